@@ -1,0 +1,393 @@
+// C ABI of the evict() prefill path (declared in include/flash_evict.h).
+//
+// Host side only: argument checks, TMA tensor-map encoding for arbitrarily
+// strided Q/K/V, kernel selection by head dimension and dtype, launches on the
+// caller's stream.  No allocation and no host synchronization on the compute
+// entry points.  The library links the CUDA runtime statically; because the
+// caller (PyTorch) has its own runtime instance, every entry point first makes
+// the device that owns the input pointer current for this runtime.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "fe_forward.cuh"
+#include "fe_replay.cuh"
+#include "fe_select.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+int64_t g_watchdog_ns = 2000000000LL;
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(FE_STATUS_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Make the device owning `ptr` current for this runtime instance.
+int bind_device(const void* ptr, int* dev_out) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return fail(FE_STATUS_INVALID, "pointer %p is not device memory", ptr);
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != a.device) {
+    e = cudaSetDevice(a.device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  }
+  if (dev_out) *dev_out = a.device;
+  return FE_STATUS_OK;
+}
+
+int padded_dim(int64_t d) { return d <= 64 ? 64 : (d <= 128 ? 128 : 0); }
+
+// TMA map over a [B, H, N, D] view with element strides s[4] (s[3] == 1),
+// box = 64 channels x 128 tokens, 128-byte swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* m, const void* ptr, const int64_t* s, int64_t B, int64_t H, int64_t N, int64_t D,
+             int dtype, const char* name) {
+  if (s[3] != 1) return fail(FE_STATUS_UNSUPPORTED, "%s: channel stride must be 1 (got %lld)", name, (long long)s[3]);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return fail(FE_STATUS_UNSUPPORTED, "%s: base pointer must be 16-byte aligned", name);
+  const int64_t ext[3] = {N, H, B};
+  const int64_t st[3] = {s[2], s[1], s[0]};
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t gstr[3];
+  int64_t fallback = D * 2;
+  for (int i = 0; i < 3; ++i) {
+    int64_t bytes = st[i] * 2;
+    if (ext[i] == 1) {
+      // Never stepped over: any legal stride works.
+      bytes = (fallback + 15) / 16 * 16;
+    }
+    if (bytes <= 0 || bytes % 16 != 0 || bytes >= (int64_t(1) << 40))
+      return fail(FE_STATUS_UNSUPPORTED, "%s: stride %lld elements is not a positive multiple of 8", name,
+                  (long long)st[i]);
+    gstr[i] = (cuuint64_t)bytes;
+    fallback = bytes * ext[i];
+  }
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  auto enc = encode_fn();
+  if (!enc) return fail(FE_STATUS_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUresult r = enc(m, dtype == FE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void*>(ptr), dims, gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FE_STATUS_UNSUPPORTED, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return FE_STATUS_OK;
+}
+
+int check_shapes(int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int dtype) {
+  if (B < 1 || Hq < 1 || Hkv < 1 || N < 1 || D < 1)
+    return fail(FE_STATUS_INVALID, "empty shape B=%lld Hq=%lld Hkv=%lld N=%lld D=%lld", (long long)B, (long long)Hq,
+                (long long)Hkv, (long long)N, (long long)D);
+  if (Hq % Hkv) return fail(FE_STATUS_INVALID, "q_heads must be divisible by kv_heads");
+  if (dtype != FE_DTYPE_F16 && dtype != FE_DTYPE_BF16) return fail(FE_STATUS_INVALID, "dtype must be f16 or bf16");
+  if (D > 256) return fail(FE_STATUS_INVALID, "channels must be <= 256");
+  if (padded_dim(D) == 0) return fail(FE_STATUS_UNSUPPORTED, "channels > 128 are not supported by the sm_100a kernels");
+  if (N > (int64_t(1) << 30) || B * Hq > (int64_t(1) << 30)) return fail(FE_STATUS_UNSUPPORTED, "problem too large");
+  return FE_STATUS_OK;
+}
+
+template <typename K>
+int set_smem(K kernel, int bytes) {
+  // One attribute call per kernel instantiation and device.
+  static int done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && done[dev] >= bytes) return FE_STATUS_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  if (dev < 64) done[dev] = bytes;
+  return FE_STATUS_OK;
+}
+
+template <bool BF16, int DP>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fe::FwdParams& p,
+               int64_t items, cudaStream_t stream) {
+  using C = fe::FwdCfg<DP>;
+  auto kern = fe::fe_fwd_kernel<BF16, DP>;
+  int rc = set_smem(kern, C::SMEM);
+  if (rc) return rc;
+  kern<<<dim3((unsigned)items), dim3(C::THREADS), C::SMEM, stream>>>(tq, tk, tv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return FE_STATUS_OK;
+}
+
+template <bool BF16, int DP>
+int launch_replay(const CUtensorMap& tq, const CUtensorMap& tk, const fe::ReplayParams& p, int64_t items,
+                  cudaStream_t stream) {
+  using C = fe::ReplayCfg<DP>;
+  auto kern = fe::fe_replay_kernel<BF16, DP>;
+  int rc = set_smem(kern, C::SMEM);
+  if (rc) return rc;
+  kern<<<dim3((unsigned)items), dim3(C::THREADS), C::SMEM, stream>>>(tq, tk, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "replay launch");
+  return FE_STATUS_OK;
+}
+
+__global__ void fe_watchdog_kernel(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    fe::mbar_init(&bar, 1);
+    fe::fence_mbar_init();
+  }
+  __syncthreads();
+  // Nothing ever arrives on `bar`: the bounded wait must give up and report.
+  fe::mbar_wait(&bar, 0, timeout_ns, &abort_flag);
+  __syncthreads();
+}
+
+}  // namespace
+
+extern "C" {
+
+int fe_abi_version(void) { return 1; }
+
+const char* fe_last_error(void) { return g_err; }
+
+void fe_set_watchdog_ns(int64_t ns) { g_watchdog_ns = ns > 0 ? ns : 2000000000LL; }
+
+int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                     const void* v, const int64_t* v_strides, void* out, float* row_stats, int64_t batch,
+                     int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype, int causal,
+                     float scale, const int32_t* query_blocks, int64_t num_query_blocks, void* stream) {
+  g_err[0] = 0;
+  int rc = check_shapes(batch, q_heads, kv_heads, tokens, channels, dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !out || !row_stats) return fail(FE_STATUS_INVALID, "null pointer");
+  if (!std::isfinite(scale)) return fail(FE_STATUS_INVALID, "scale must be finite");
+  if (reinterpret_cast<uintptr_t>(out) % 16) return fail(FE_STATUS_UNSUPPORTED, "out must be 16-byte aligned");
+  rc = bind_device(q, nullptr);
+  if (rc) return rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q"))) return rc;
+  if ((rc = make_map(&tk, k, k_strides, batch, kv_heads, tokens, channels, dtype, "k"))) return rc;
+  if ((rc = make_map(&tv, v, v_strides, batch, kv_heads, tokens, channels, dtype, "v"))) return rc;
+  const int64_t nblk_all = (tokens + FE_QUERY_BLOCK - 1) / FE_QUERY_BLOCK;
+  if (query_blocks && (num_query_blocks < 0 || num_query_blocks > nblk_all))
+    return fail(FE_STATUS_INVALID, "num_query_blocks out of range");
+  fe::FwdParams p;
+  p.out = out;
+  p.row_stats = row_stats;
+  p.blocks = query_blocks;
+  p.num_blocks = (int)(query_blocks ? num_query_blocks : nblk_all);
+  p.B = (int)batch;
+  p.Hq = (int)q_heads;
+  p.Hkv = (int)kv_heads;
+  p.N = (int)tokens;
+  p.D = (int)channels;
+  p.G = (int)(q_heads / kv_heads);
+  p.sc = (float)((double)scale * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  p.timeout_ns = (uint64_t)g_watchdog_ns;
+  const int64_t items = (int64_t)p.num_blocks * batch * q_heads;
+  if (items == 0) return FE_STATUS_OK;
+  if (items > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int dp = padded_dim(channels);
+  if (dtype == FE_DTYPE_BF16)
+    return dp == 64 ? launch_fwd<true, 64>(tq, tk, tv, p, items, s) : launch_fwd<true, 128>(tq, tk, tv, p, items, s);
+  return dp == 64 ? launch_fwd<false, 64>(tq, tk, tv, p, items, s) : launch_fwd<false, 128>(tq, tk, tv, p, items, s);
+}
+
+int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+                     const int64_t* v_strides, const float* row_stats, float* importance, int64_t batch,
+                     int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype, int causal,
+                     float scale, float recency_decay, int64_t observation_window, int value_weighted,
+                     const int32_t* query_blocks, int64_t num_query_blocks, void* stream) {
+  g_err[0] = 0;
+  int rc = check_shapes(batch, q_heads, kv_heads, tokens, channels, dtype);
+  if (rc) return rc;
+  if (!q || !k || !v || !row_stats || !importance) return fail(FE_STATUS_INVALID, "null pointer");
+  if (!std::isfinite(scale)) return fail(FE_STATUS_INVALID, "scale must be finite");
+  if (!std::isfinite(recency_decay) || recency_decay < 0)
+    return fail(FE_STATUS_INVALID, "recency_decay must be finite and nonnegative");
+  if (observation_window < 0) return fail(FE_STATUS_INVALID, "observation_window must be >= 0");
+  if (v_strides[3] != 1) return fail(FE_STATUS_UNSUPPORTED, "v: channel stride must be 1");
+  rc = bind_device(q, nullptr);
+  if (rc) return rc;
+  CUtensorMap tq, tk;
+  if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q"))) return rc;
+  if ((rc = make_map(&tk, k, k_strides, batch, kv_heads, tokens, channels, dtype, "k"))) return rc;
+  const int64_t nblk_all = (tokens + FE_QUERY_BLOCK - 1) / FE_QUERY_BLOCK;
+  if (query_blocks) {
+    if (num_query_blocks < 0 || num_query_blocks > nblk_all)
+      return fail(FE_STATUS_INVALID, "num_query_blocks out of range");
+    if (nblk_all > fe::ReplayCfg<64>::MAP_WORDS * 32)
+      return fail(FE_STATUS_UNSUPPORTED, "query-block lists are limited to %d blocks", fe::ReplayCfg<64>::MAP_WORDS * 32);
+  }
+  fe::ReplayParams p;
+  p.row_stats = row_stats;
+  p.importance = importance;
+  p.v = reinterpret_cast<const uint8_t*>(v);
+  p.v_sb = v_strides[0];
+  p.v_sh = v_strides[1];
+  p.v_sn = v_strides[2];
+  p.blocks = query_blocks;
+  p.num_blocks = (int)(query_blocks ? num_query_blocks : nblk_all);
+  p.B = (int)batch;
+  p.Hq = (int)q_heads;
+  p.Hkv = (int)kv_heads;
+  p.N = (int)tokens;
+  p.D = (int)channels;
+  p.G = (int)(q_heads / kv_heads);
+  p.sc = (float)((double)scale * 1.4426950408889634);
+  p.decay_log2 = (float)((double)recency_decay * 1.4426950408889634);
+  const int64_t W = (observation_window == 0 || observation_window > tokens) ? tokens : observation_window;
+  int64_t s_lo = tokens - W;
+  if (recency_decay > 0) {
+    // Rows farther than this from the end have FP32 weights below 2^-127.
+    const double reach = 127.0 / ((double)recency_decay * 1.4426950408889634);
+    if (reach < (double)tokens) {
+      const int64_t cut = tokens - 1 - (int64_t)std::floor(reach);
+      if (cut > s_lo) s_lo = cut;
+    }
+  }
+  p.s_lo = (int)s_lo;
+  p.causal = causal ? 1 : 0;
+  p.weighted = value_weighted ? 1 : 0;
+  p.timeout_ns = (uint64_t)g_watchdog_ns;
+  const int64_t items = ((tokens + 127) / 128) * batch * kv_heads;
+  if (items > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int dp = padded_dim(channels);
+  if (dtype == FE_DTYPE_BF16)
+    return dp == 64 ? launch_replay<true, 64>(tq, tk, p, items, s) : launch_replay<true, 128>(tq, tk, p, items, s);
+  return dp == 64 ? launch_replay<false, 64>(tq, tk, p, items, s) : launch_replay<false, 128>(tq, tk, p, items, s);
+}
+
+int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
+                     int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, void* stream) {
+  g_err[0] = 0;
+  if (rows < 0 || tokens < 1) return fail(FE_STATUS_INVALID, "bad rows/tokens");
+  if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+  if (recent < 0 || recent > budget) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
+  if (pool_kernel < 1 || pool_kernel % 2 != 1) return fail(FE_STATUS_INVALID, "pool_kernel must be a positive odd integer");
+  if (rows == 0) return FE_STATUS_OK;
+  if (!importance || !indices || !mask) return fail(FE_STATUS_INVALID, "null pointer");
+  int rc = bind_device(importance, nullptr);
+  if (rc) return rc;
+  const int64_t P = tokens - recent;
+  const int64_t max_slice = 49152;  // keys per CTA held in shared memory (192 KiB)
+  int cl = 1;
+  while (cl < 16 && (P + cl - 1) / cl > max_slice) cl *= 2;
+  if ((P + cl - 1) / cl > max_slice)
+    return fail(FE_STATUS_UNSUPPORTED, "sequence length %lld exceeds the selection limit (%lld)", (long long)tokens,
+                (long long)(max_slice * 16));
+  int64_t chunk = (P + cl - 1) / cl;
+  if (chunk < 1) chunk = 1;
+  if (rows * cl > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "too many rows");
+  fe::SelectParams p;
+  p.importance = importance;
+  p.N = tokens;
+  p.budget = budget;
+  p.recent = recent;
+  p.pool = (int)pool_kernel;
+  p.indices = indices;
+  p.mask = mask;
+  p.mask_evict = mask_evict ? 1 : 0;
+  p.chunk = chunk;
+  const int smem = (int)(chunk * 4);
+  rc = set_smem(fe::fe_select_kernel, smem < 49152 ? 49152 : smem);
+  if (rc) return rc;
+  if (cl > 8) {
+    cudaError_t e = cudaFuncSetAttribute(fe::fe_select_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_fail(e, "cluster attribute");
+  }
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)(rows * cl));
+  cfg.blockDim = dim3(fe::SEL_THREADS);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cl;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fe::fe_select_kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "selection launch");
+  return FE_STATUS_OK;
+}
+
+int fe_evict(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+             const int64_t* v_strides, void* out, float* importance, int64_t* indices, uint8_t* mask,
+             float* row_stats, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels,
+             int dtype, int causal, float scale, float recency_decay, int64_t observation_window, int value_weighted,
+             int64_t budget, int64_t recent, int64_t pool_kernel, void* stream) {
+  if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+  if (recent < 0 || recent > budget) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
+  if (pool_kernel < 1 || pool_kernel % 2 != 1) return fail(FE_STATUS_INVALID, "pool_kernel must be a positive odd integer");
+  int rc = fe_attention_fwd(q, q_strides, k, k_strides, v, v_strides, out, row_stats, batch, q_heads, kv_heads, tokens,
+                            channels, dtype, causal, scale, nullptr, 0, stream);
+  if (rc) return rc;
+  rc = fe_replay_scores(q, q_strides, k, k_strides, v, v_strides, row_stats, importance, batch, q_heads, kv_heads,
+                        tokens, channels, dtype, causal, scale, recency_decay, observation_window, value_weighted,
+                        nullptr, 0, stream);
+  if (rc) return rc;
+  return fe_select_tokens(importance, batch * kv_heads, tokens, budget, recent, pool_kernel, indices, mask, 1, stream);
+}
+
+int fe_device_status(int device, int clear, int* status_out) {
+  g_err[0] = 0;
+  int cur = -1;
+  cudaGetDevice(&cur);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int st = 0;
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&st, fe::g_status, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(fe::g_status, &zero, sizeof(int));
+  }
+  if (cur >= 0 && cur != device) cudaSetDevice(cur);
+  if (e != cudaSuccess) return cuda_fail(e, "status read");
+  if (status_out) *status_out = st;
+  return FE_STATUS_OK;
+}
+
+int fe_watchdog_selftest(int64_t timeout_ns, void* stream) {
+  g_err[0] = 0;
+  if (timeout_ns <= 0 || timeout_ns > 10000000000LL) return fail(FE_STATUS_INVALID, "timeout out of range");
+  fe_watchdog_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "watchdog launch");
+  return FE_STATUS_OK;
+}
+
+}  // extern "C"

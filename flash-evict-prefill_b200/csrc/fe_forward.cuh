@@ -1,0 +1,376 @@
+// Attention forward (traversal 1) for sm_100a.
+//
+// Restates the first KV traversal of `_prefill` (flash_evict/prefill.py:23-60):
+// online softmax in the log2 domain (logits * scale * log2e), P cast to the
+// input dtype before the PV product, FP32 row max m and row sum l; plus the
+// store of O = acc / l (prefill.py:59-60).  In addition it writes the final
+// (m, l) of every row so the replay kernel can normalise without a second
+// online pass.
+//
+// CTA work unit: one query block = two 128-row query tiles (Q0, Q1) of one
+// query head.  KV tiles are 128 keys.  Roles (320 threads):
+//   warps 0-3  softmax for Q0 (thread = TMEM lane = query row)
+//   warps 4-7  softmax for Q1
+//   warp  8    TMA producer (Q once, K/V through a STAGES-deep ring)
+//   warp  9    tcgen05 issuer (one thread) and TMEM owner
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+DP), O1 after.
+// P (16-bit) overwrites the first 64 columns of its S tile and feeds the PV
+// MMA straight from TMEM (A operand in TMEM, V as an MN-major B operand).
+//
+// Issue order on the tensor pipe per KV tile j:
+//   PV0(j), S0(j+1), PV1(j), S1(j+1)
+// so that when softmax t observes S_t(j+1) complete, PV_t(j) has completed
+// too and O_t may be rescaled in place.  The O rescale is lazy: the max used
+// for exponentiation only moves when the true max exceeds it by more than
+// 2^8, which keeps P <= 256 and makes rescales rare.
+#pragma once
+
+#include "fe_ptx.cuh"
+
+namespace fe {
+
+struct FwdParams {
+  void* out;          // [B, Hq, N, D] contiguous, input dtype
+  float* row_stats;   // [B, Hq, N, 2] {m, l}
+  const int32_t* blocks;  // optional list of query blocks (256 rows), heaviest first
+  int num_blocks;     // length of `blocks`, or number of blocks when blocks == nullptr
+  int B, Hq, Hkv, N, D, G;
+  float sc;           // scale * log2(e)
+  int causal;
+  uint64_t timeout_ns;
+};
+
+template <int DP>
+struct FwdCfg {
+  static constexpr int TILE = 128 * DP * 2;        // bytes of one 128-row tile
+  static constexpr int STAGES = (DP <= 64) ? 4 : 2;
+  static constexpr int NCH = DP / 64;              // 64-column swizzle chunks
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = 2 * TILE;
+  static constexpr int OFF_V = OFF_K + STAGES * TILE;
+  static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
+  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
+  static constexpr int NBAR = 1 + 4 * STAGES + 7;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment slack
+  static constexpr int THREADS = 320;
+};
+
+__device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
+
+template <bool BF16, int DP>
+__global__ void __launch_bounds__(320, 1)
+    fe_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, const FwdParams p) {
+  using C = FwdCfg<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + C::STAGES;
+  uint64_t* k_empty = v_full + C::STAGES;
+  uint64_t* v_empty = k_empty + C::STAGES;
+  uint64_t* s_full = v_empty + C::STAGES;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+
+  // ---- work item: (query block, b, hkv, g), heaviest query block first ----
+  int item = blockIdx.x;
+  const int g = item % p.G;
+  item /= p.G;
+  const int hkv = item % p.Hkv;
+  item /= p.Hkv;
+  const int b = item % p.B;
+  const int rank = item / p.B;
+  int blk;
+  if (p.blocks != nullptr) {
+    blk = p.blocks[rank];
+  } else {
+    blk = p.causal ? (p.num_blocks - 1 - rank) : rank;
+  }
+  const int hq = hkv * p.G + g;
+  const int nkv = (p.N + 127) / 128;
+  const int row0 = blk * 256;
+  const int row1 = row0 + 128;
+  const int n0 = (row0 < p.N) ? (p.causal ? min(nkv, row0 / 128 + 1) : nkv) : 0;
+  const int n1 = (row1 < p.N) ? (p.causal ? min(nkv, row1 / 128 + 1) : nkv) : 0;
+  const int nmax = max(n0, n1);
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_full[t], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    __syncwarp();
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint64_t TO = p.timeout_ns;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0 && nmax > 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      uint32_t loads[C::STAGES];
+      for (int s = 0; s < C::STAGES; ++s) loads[s] = 0;
+      mbar_expect_tx(q_full, ((n0 > 0) + (n1 > 0)) * C::TILE);
+      for (int c = 0; c < C::NCH; ++c) {
+        if (n0 > 0) tma_load_4d(smem + C::OFF_Q + c * 16384, &tq, q_full, c * 64, row0, hq, b);
+        if (n1 > 0) tma_load_4d(smem + C::OFF_Q + C::TILE + c * 16384, &tq, q_full, c * 64, row1, hq, b);
+      }
+      bool ok = true;
+      for (int j = 0; j < nmax && ok; ++j) {
+        const int s = j % C::STAGES;
+        const uint32_t use = j / C::STAGES;
+        if (use > 0) ok = mbar_wait(&k_empty[s], (use - 1) & 1, TO, abort_flag);
+        if (!ok) break;
+        mbar_expect_tx(&k_full[s], C::TILE);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(smem + C::OFF_K + s * C::TILE + c * 16384, &tk, &k_full[s], c * 64, j * 128, hkv, b);
+        if (use > 0) ok = mbar_wait(&v_empty[s], (use - 1) & 1, TO, abort_flag);
+        if (!ok) {
+          loads[s] = use * 2 + 1;  // K of this use in flight, V not issued
+          break;
+        }
+        mbar_expect_tx(&v_full[s], C::TILE);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(smem + C::OFF_V + s * C::TILE + c * 16384, &tv, &v_full[s], c * 64, j * 128, hkv, b);
+        loads[s] = use * 2 + 2;
+      }
+      // Never leave the CTA with a TMA write in flight: wait for the last load
+      // issued into each stage (already complete on the normal path).
+      mbar_wait(q_full, 0, TO, abort_flag);
+      for (int s = 0; s < C::STAGES; ++s) {
+        if (loads[s] == 0) continue;
+        const uint32_t use = (loads[s] - 1) / 2;
+        mbar_wait(&k_full[s], use & 1, TO, abort_flag);
+        if (loads[s] % 2 == 0) mbar_wait(&v_full[s], use & 1, TO, abort_flag);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer --
+    if (lane == 0 && nmax > 0) {
+      constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false);
+      constexpr uint32_t ID_PV = idesc_f16(128, DP, BF16, true);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
+      const uint32_t v_addr = smem_u32(smem + C::OFF_V);
+      auto issue_s = [&](int t, int s) {
+        const uint32_t qa = q_addr + t * C::TILE;
+        const uint32_t ka = k_addr + s * C::TILE;
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_ss(tmem + t * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024), ID_S,
+                  kk > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int s, int j) {
+        const uint32_t va = v_addr + s * C::TILE;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          umma_ts(tmem + 256 + t * DP, tmem + t * 128 + kk * 8, smem_desc_sw128(va + kk * 2048, 16384, 1024), ID_PV,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, TO, abort_flag);
+      if (ok) ok = mbar_wait(&k_full[0], 0, TO, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        if (n0 > 0) {
+          issue_s(0, 0);
+          umma_commit(&s_full[0]);
+        }
+        if (n1 > 0) {
+          issue_s(1, 0);
+          umma_commit(&s_full[1]);
+        }
+        if (C::STAGES < nmax) umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nmax && ok; ++j) {
+        const int s = j % C::STAGES;
+        const int s2 = (j + 1) % C::STAGES;
+        const bool next = (j + 1 < nmax);
+        bool k_next_ready = false;
+        ok = mbar_wait(&v_full[s], (j / C::STAGES) & 1, TO, abort_flag);
+        if (!ok) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int nt = t == 0 ? n0 : n1;
+          if (j >= nt) continue;
+          ok = mbar_wait(&p_full[t], j & 1, TO, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(t, s, j);
+          if (j + 1 < nt) {
+            if (!k_next_ready) {
+              ok = mbar_wait(&k_full[s2], ((j + 1) / C::STAGES) & 1, TO, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+              k_next_ready = true;
+            }
+            issue_s(t, s2);
+            umma_commit(&s_full[t]);
+          } else {
+            umma_commit(&o_full[t]);
+          }
+        }
+        if (!ok) break;
+        // Release the stages only when the producer will refill them.
+        if (j + C::STAGES < nmax) umma_commit(&v_empty[s]);
+        if (next && (j + 1 + C::STAGES < nmax)) umma_commit(&k_empty[s2]);
+      }
+      // Drain: every MMA issued above has completed once this returns.
+      umma_commit(drain);
+      mbar_wait(drain, 0, TO, abort_flag);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax --
+    const int t = warp >> 2;
+    const int nt = t == 0 ? n0 : n1;
+    const int rbase = t == 0 ? row0 : row1;
+    const int r = ((warp & 3) << 5) + static_cast<int>(lane);
+    const int row = rbase + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) << 5) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + 256 + t * DP;
+    const float sc = p.sc;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      ok = warp_all(mbar_wait(&s_full[t], j & 1, TO, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+        tmem_ld64_sync(tS, xr);
+        tmem_ld64_sync(tS + 64, xr + 64);
+      }
+      const int kbase = j * 128;
+      const bool masked = (kbase + 128 > p.N) || (p.causal && kbase + 127 > rbase);
+      float mx = -INFINITY;
+      if (masked) {
+        const int lim = p.causal ? min(p.N - 1, row) : (p.N - 1);
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] = (kbase + c <= lim) ? x[c] * sc : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] = x[c] * sc;
+          mx = fmaxf(mx, x[c]);
+        }
+      }
+      const float m_new = fmaxf(m_used, mx);
+      if (j == 0) {
+        m_used = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
+        // Rescale this warp's O rows; PV_t(j-1) is complete (see header).
+        const float f = ex2_approx(m_used - m_new);
+        l *= f;
+        m_used = m_new;
+#pragma unroll 1
+        for (int c0 = 0; c0 < DP; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_sync(tO + c0, o);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+          tmem_st32(tO + c0, o);
+        }
+        tmem_wait_st();
+      }
+      float sum0 = 0.f, sum1 = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = ex2_approx(x[2 * c] - m_used);
+        const float p1 = ex2_approx(x[2 * c + 1] - m_used);
+        sum0 += p0;
+        sum1 += p1;
+        pk[c] = pack2<BF16>(p0, p1);
+      }
+      l += sum0 + sum1;
+      tmem_st32(tS, pk);
+      tmem_st32(tS + 32, pk + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (nt > 0 && ok) {
+      ok = warp_all(mbar_wait(&o_full[t], 0, TO, abort_flag));
+      if (ok) {
+        tc_fence_after();
+        const bool live = row < p.N;
+        if (live) {
+          float2* st = reinterpret_cast<float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hq) * p.N + row;
+          *st = make_float2(m_used, l);
+        }
+        const float inv = 1.0f / l;
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        T* orow = reinterpret_cast<T*>(p.out) + ((static_cast<size_t>(b) * p.Hq + hq) * p.N + row) * p.D;
+        const bool vec = (p.D % 8) == 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < DP; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_sync(tO + c0, o);
+          if (live && c0 < p.D) {
+            uint32_t w[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              w[c] = pack2<BF16>(__uint_as_float(o[2 * c]) * inv, __uint_as_float(o[2 * c + 1]) * inv);
+            if (vec) {
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                if (c0 + q4 * 8 < p.D)
+                  *reinterpret_cast<uint4*>(orow + c0 + q4 * 8) =
+                      make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+              }
+            } else {
+              const uint16_t* h = reinterpret_cast<const uint16_t*>(w);
+              for (int c = 0; c < 32 && c0 + c < p.D; ++c) reinterpret_cast<uint16_t*>(orow)[c0 + c] = h[c];
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fe

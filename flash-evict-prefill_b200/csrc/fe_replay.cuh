@@ -1,0 +1,316 @@
+// Exact per-KV-token importance by replay (traversal 2) for sm_100a.
+//
+// Restates the replay loop of `_prefill` (flash_evict/prefill.py:61-83) and
+// the zero-initialised score buffer it accumulates into (prefill.py:129):
+//   I[b,hkv,k] = ||v_k||_1 * sum_{g,q} w_q * exp2(s_qk*scale*log2e - m_q) / l_q
+//   w_q = exp(decay * (q - (N-1))) * [q >= N - W]
+// but key-stationary instead of query-stationary: one CTA owns 128 keys of
+// one (b, hkv) and walks every scored (query tile, group head) pair, computing
+// S^T = K Q^T on the tensor cores with keys on the TMEM lanes.  Each thread
+// owns one key, so the reduction over queries is a register sum with no
+// shuffles and no atomics, and every importance element is stored exactly
+// once (deterministic, no zero-fill launch).
+//
+// The per-query normaliser and weight fold into one exponent bias:
+//   w_q / l_q * exp2(x - m_q) = exp2(x - bias_q),
+//   bias_q = m_q + log2(l_q) - decay*log2(e)*(q - (N-1))
+// with bias_q = +inf for rows outside the window or past N.  Query tiles whose
+// every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
+//
+// Roles (192 threads): warps 0-3 reduce (thread = key), warp 4 TMA producer,
+// warp 5 tcgen05 issuer and TMEM owner.  TMEM: two 128-column S^T buffers.
+#pragma once
+
+#include "fe_ptx.cuh"
+
+namespace fe {
+
+struct ReplayParams {
+  const float* row_stats;   // [B, Hq, N, 2]
+  float* importance;        // [B, Hkv, N]
+  const uint8_t* v;         // V base pointer (bytes)
+  int64_t v_sb, v_sh, v_sn; // V strides in elements
+  const int32_t* blocks;    // optional query-block list (256-row blocks)
+  int num_blocks;
+  int B, Hq, Hkv, N, D, G;
+  float sc;                 // scale * log2(e)
+  float decay_log2;         // recency_decay * log2(e)
+  int s_lo;                 // first scored row (window and underflow cut)
+  int causal, weighted;
+  uint64_t timeout_ns;
+};
+
+template <int DP>
+struct ReplayCfg {
+  static constexpr int TILE = 128 * DP * 2;
+  static constexpr int QST = 2;                     // Q tile ring depth
+  static constexpr int NCH = DP / 64;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_Q = TILE;
+  static constexpr int OFF_BIAS = OFF_Q + QST * TILE;     // float[4 warps][128]
+  static constexpr int OFF_MAP = OFF_BIAS + 4 * 128 * 4;  // uint32 bitmap of listed query blocks
+  static constexpr int MAP_WORDS = 256;                   // up to 8192 blocks
+  static constexpr int OFF_BAR = OFF_MAP + MAP_WORDS * 4;
+  // k_full, q_full[QST], q_empty[QST], s_full[2], s_free[2], drain
+  static constexpr int NBAR = 1 + 2 * QST + 5;
+  static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
+  static constexpr int THREADS = 192;
+};
+
+// Iterates the CTA's (query tile, head-in-group) items in a fixed order.
+struct ReplayItems {
+  int qt, qt_end, g, G;
+  const uint32_t* map;  // nullptr: every query tile
+  __device__ __forceinline__ bool listed(int tile) const {
+    if (map == nullptr) return true;
+    const int blk = tile >> 1;
+    return (map[blk >> 5] >> (blk & 31)) & 1u;
+  }
+  __device__ __forceinline__ void init(int lo, int hi, int groups, const uint32_t* m) {
+    qt = lo;
+    qt_end = hi;
+    g = 0;
+    G = groups;
+    map = m;
+    while (qt < qt_end && !listed(qt)) ++qt;
+  }
+  __device__ __forceinline__ bool valid() const { return qt < qt_end; }
+  __device__ __forceinline__ void next() {
+    if (++g == G) {
+      g = 0;
+      ++qt;
+      while (qt < qt_end && !listed(qt)) ++qt;
+    }
+  }
+};
+
+template <bool BF16, int DP>
+__global__ void __launch_bounds__(192, 2)
+    fe_replay_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const ReplayParams p) {
+  using C = ReplayCfg<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* sbias = reinterpret_cast<float*>(smem + C::OFF_BIAS);
+  uint32_t* smap = reinterpret_cast<uint32_t*>(smem + C::OFF_MAP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* k_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = q_full + C::QST;
+  uint64_t* s_full = q_empty + C::QST;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* drain = s_free + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+
+  // ---- work item: (key tile, b, hkv); key tile 0 (most causal work) first ----
+  int item = blockIdx.x;
+  const int hkv = item % p.Hkv;
+  item /= p.Hkv;
+  const int b = item % p.B;
+  const int kt = item / p.B;
+  const int nqt = (p.N + 127) / 128;
+  const int qt_lo = max(p.s_lo / 128, p.causal ? kt : 0);
+  const uint32_t* map = nullptr;
+
+  if (p.blocks != nullptr) {
+    for (int i = threadIdx.x; i < C::MAP_WORDS; i += blockDim.x) smap[i] = 0;
+  }
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    mbar_init(k_full, 1);
+    for (int s = 0; s < C::QST; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    __syncwarp();
+    tmem_alloc(tmem_holder, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (p.blocks != nullptr) {
+    for (int i = threadIdx.x; i < p.num_blocks; i += blockDim.x) {
+      const int blk = p.blocks[i];
+      atomicOr(&smap[blk >> 5], 1u << (blk & 31));
+    }
+    __syncthreads();
+    map = smap;
+  }
+  const uint32_t tmem = *tmem_holder;
+  const uint64_t TO = p.timeout_ns;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer --
+    if (lane == 0) {
+      tma_prefetch_desc(&tq);
+      tma_prefetch_desc(&tk);
+      ReplayItems it;
+      it.init(qt_lo, nqt, p.G, map);
+      uint32_t issued = 0;
+      if (it.valid()) {
+        mbar_expect_tx(k_full, C::TILE);
+        for (int c = 0; c < C::NCH; ++c)
+          tma_load_4d(smem + C::OFF_K + c * 16384, &tk, k_full, c * 64, kt * 128, hkv, b);
+        bool ok = true;
+        for (; it.valid(); it.next(), ++issued) {
+          const int s = issued % C::QST;
+          const uint32_t use = issued / C::QST;
+          if (use > 0) ok = mbar_wait(&q_empty[s], (use - 1) & 1, TO, abort_flag);
+          if (!ok) break;
+          mbar_expect_tx(&q_full[s], C::TILE);
+          const int hq = hkv * p.G + it.g;
+          for (int c = 0; c < C::NCH; ++c)
+            tma_load_4d(smem + C::OFF_Q + s * C::TILE + c * 16384, &tq, &q_full[s], c * 64, it.qt * 128, hq, b);
+        }
+        // Wait for the last load of each ring slot and for K before exiting.
+        mbar_wait(k_full, 0, TO, abort_flag);
+        for (uint32_t i = (issued > C::QST ? issued - C::QST : 0); i < issued; ++i)
+          mbar_wait(&q_full[i % C::QST], (i / C::QST) & 1, TO, abort_flag);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false);
+      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
+      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      ReplayItems it;
+      it.init(qt_lo, nqt, p.G, map);
+      if (it.valid()) {
+        bool ok = mbar_wait(k_full, 0, TO, abort_flag);
+        uint32_t i = 0;
+        for (; it.valid() && ok; it.next(), ++i) {
+          const int s = i % C::QST;
+          const int sb = i & 1;
+          ok = mbar_wait(&q_full[s], (i / C::QST) & 1, TO, abort_flag);
+          if (!ok) break;
+          if (i >= 2) ok = mbar_wait(&s_free[sb], ((i >> 1) - 1) & 1, TO, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t qa = q_addr + s * C::TILE;
+#pragma unroll
+          for (int kk = 0; kk < DP / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_ss(tmem + sb * 128, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(qa + off, 16, 1024),
+                    ID_S, kk > 0);
+          }
+          umma_commit(&s_full[sb]);
+          umma_commit(&q_empty[s]);
+        }
+        umma_commit(drain);
+        mbar_wait(drain, 0, TO, abort_flag);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- reduce --
+    const int kr = (warp << 5) + static_cast<int>(lane);  // key row in tile
+    const int key = kt * 128 + kr;
+    const uint32_t lane_off = static_cast<uint32_t>(warp << 5) << 16;
+    const float sc = p.sc;
+    float* wbias = sbias + warp * 128;
+    double acc = 0.0;
+    ReplayItems it;
+    it.init(qt_lo, nqt, p.G, map);
+    uint32_t i = 0;
+    bool ok = true;
+    for (; it.valid(); it.next(), ++i) {
+      const int sb = i & 1;
+      // Exponent bias of the item's 128 query columns; each warp keeps its own
+      // copy (lane l fills columns l, l+32, l+64, l+96) so the warpgroup needs
+      // no cross-warp barrier.
+      __syncwarp();
+      {
+        const int hq = hkv * p.G + it.g;
+        const float2* st = reinterpret_cast<const float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hq) * p.N;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = static_cast<int>(lane) + 32 * u;
+          const int q = it.qt * 128 + c;
+          float bias = INFINITY;
+          if (q < p.N && q >= p.s_lo) {
+            const float2 ml = st[q];
+            bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml.x + log2f(ml.y));
+          }
+          wbias[c] = bias;
+        }
+      }
+      __syncwarp();
+      ok = warp_all(mbar_wait(&s_full[sb], (i >> 1) & 1, TO, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float x[128];
+      {
+        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
+        tmem_ld64_sync(tmem + lane_off + sb * 128, xr);
+        tmem_ld64_sync(tmem + lane_off + sb * 128 + 64, xr + 64);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      const float4* bias4 = reinterpret_cast<const float4*>(wbias);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      if (p.causal && it.qt == kt) {
+        // Diagonal tile: query column c contributes only when c >= kr.
+#pragma unroll
+        for (int c4 = 0; c4 < 32; ++c4) {
+          const float4 bb = bias4[c4];
+          const int c = c4 * 4;
+          a0 += (c + 0 >= kr) ? ex2_approx(fmaf(x[c + 0], sc, -bb.x)) : 0.f;
+          a1 += (c + 1 >= kr) ? ex2_approx(fmaf(x[c + 1], sc, -bb.y)) : 0.f;
+          a2 += (c + 2 >= kr) ? ex2_approx(fmaf(x[c + 2], sc, -bb.z)) : 0.f;
+          a3 += (c + 3 >= kr) ? ex2_approx(fmaf(x[c + 3], sc, -bb.w)) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int c4 = 0; c4 < 32; ++c4) {
+          const float4 bb = bias4[c4];
+          const int c = c4 * 4;
+          a0 += ex2_approx(fmaf(x[c + 0], sc, -bb.x));
+          a1 += ex2_approx(fmaf(x[c + 1], sc, -bb.y));
+          a2 += ex2_approx(fmaf(x[c + 2], sc, -bb.z));
+          a3 += ex2_approx(fmaf(x[c + 3], sc, -bb.w));
+        }
+      }
+      acc += static_cast<double>((a0 + a1) + (a2 + a3));
+    }
+    if (ok && key < p.N) {
+      float vn = 1.0f;
+      if (p.weighted) {
+        using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+        const T* vrow = reinterpret_cast<const T*>(p.v) + b * p.v_sb + hkv * p.v_sh + static_cast<int64_t>(key) * p.v_sn;
+        float s = 0.f;
+        for (int d = 0; d < p.D; ++d) {
+          float x;
+          if constexpr (BF16) x = __bfloat162float(vrow[d]);
+          else x = __half2float(vrow[d]);
+          s += fabsf(x);
+        }
+        vn = s;
+      }
+      p.importance[(static_cast<size_t>(b) * p.Hkv + hkv) * p.N + key] = static_cast<float>(acc) * vn;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace fe

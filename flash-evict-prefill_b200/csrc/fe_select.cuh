@@ -1,0 +1,264 @@
+// Token selection: SnapKV-style pooling, exact top-k by radix select, and the
+// keep/evict mask, in one launch.
+//
+// Restates `select_tokens` (flash_evict/prefill.py:140-170):
+//   past   = importance[:, :N-recent]
+//   pooled = avg_pool1d(past, pool_kernel, stride 1, pad pool_kernel//2)
+//            (zero padding counted in the divisor), only if pool_kernel > 1 and
+//            budget > recent (prefill.py:161-163)
+//   keep the budget-recent largest pooled values plus the suffix [N-recent, N)
+//   indices ascending (prefill.py:164-168), mask by scatter (prefill.py:169).
+// The reference's tie order is torch.topk's (unspecified).  This kernel fixes
+// it: larger value first, among equal values the lower index; NaN is the
+// largest value and -0.0 equals +0.0.
+//
+// One thread-block cluster of C CTAs per row; CTA r holds a contiguous slice
+// of the past region as order-preserving uint32 keys in shared memory.  The
+// (budget-recent)-th largest key is found MSB-first with four 8-bit radix
+// passes whose histograms are merged through distributed shared memory.
+// Compaction walks each slice in index order (ballot/popc scans), so indices
+// come out already sorted; the cluster exchanges per-CTA counts for offsets.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "fe_ptx.cuh"
+
+namespace fe {
+
+namespace cg = cooperative_groups;
+
+struct SelectParams {
+  const float* importance;  // [rows, N]
+  int64_t N, budget, recent;
+  int pool;
+  int64_t* indices;  // [rows, budget]
+  uint8_t* mask;     // [rows, N]
+  int mask_evict;
+  int64_t chunk;     // slice length per CTA
+};
+
+constexpr int SEL_THREADS = 1024;
+constexpr int SEL_WARPS = SEL_THREADS / 32;
+
+// Order-preserving map float -> uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t order_key(float x) {
+  if (x != x) return 0xFFFFFFFFu;  // NaN sorts above +inf
+  if (x == 0.0f) x = 0.0f;         // -0.0 ties with +0.0
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Block-wide exclusive scan of one 0/1 flag per thread in index order.
+// Returns this thread's exclusive prefix; *total receives the block sum.
+__device__ __forceinline__ int block_flag_scan(bool flag, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t bal = __ballot_sync(0xffffffffu, flag);
+  const int in_warp = __popc(bal & ((1u << lane) - 1u));
+  if (lane == 0) warp_sums[warp] = __popc(bal);
+  __syncthreads();
+  if (warp == 0) {
+    int v = (lane < SEL_WARPS) ? warp_sums[lane] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane < SEL_WARPS) warp_sums[32 + lane] = incl - v;
+    if (lane == 31) warp_sums[64] = incl;
+  }
+  __syncthreads();
+  const int res = warp_sums[32 + warp] + in_warp;
+  *total = warp_sums[64];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const SelectParams p) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int crank = static_cast<int>(cluster.block_rank());
+  const int64_t row = blockIdx.x / C;
+
+  extern __shared__ uint32_t keys[];
+  __shared__ uint32_t hist[2][256];
+  __shared__ uint32_t tot[256];
+  __shared__ int warp_sums[72];
+  __shared__ uint32_t sel_digit, sel_krem;
+  __shared__ long long counts[2];  // this CTA's {greater, equal} counts
+
+  const int64_t N = p.N;
+  const int64_t P = N - p.recent;
+  const int64_t kk = p.budget - p.recent;
+  const float* imp = p.importance + row * N;
+  int64_t* out_idx = p.indices + row * p.budget;
+  uint8_t* out_mask = p.mask + row * N;
+  const uint8_t keep_v = p.mask_evict ? 0 : 1;
+  const uint8_t evict_v = p.mask_evict ? 1 : 0;
+
+  const int64_t lo = min(P, static_cast<int64_t>(crank) * p.chunk);
+  const int64_t hi = min(P, lo + p.chunk);
+  const int len = static_cast<int>(hi - lo);
+
+  // Reserved suffix: always kept, placed after the budget-recent past picks.
+  if (crank == 0) {
+    for (int64_t j = threadIdx.x; j < p.recent; j += SEL_THREADS) {
+      out_idx[kk + j] = P + j;
+      out_mask[P + j] = keep_v;
+    }
+  }
+  if (kk == 0) {
+    for (int i = threadIdx.x; i < len; i += SEL_THREADS) out_mask[lo + i] = evict_v;
+    return;
+  }
+
+  // ---- keys of this slice (pooled if requested) ----
+  const bool pooled = p.pool > 1;
+  const int r = p.pool / 2;
+  for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+    const int64_t gi = lo + i;
+    float x;
+    if (pooled) {
+      // Same accumulation as avg_pool1d: taps left to right inside the row,
+      // padding contributes nothing, divisor = kernel size.
+      float s = 0.f;
+      const int64_t a = gi - r > 0 ? gi - r : 0;
+      const int64_t e = gi + r + 1 < P ? gi + r + 1 : P;
+      for (int64_t t = a; t < e; ++t) s = __fadd_rn(s, imp[t]);
+      x = __fdiv_rn(s, static_cast<float>(p.pool));
+    } else {
+      x = imp[gi];
+    }
+    keys[i] = order_key(x);
+  }
+  for (int i = threadIdx.x; i < 512; i += SEL_THREADS) (&hist[0][0])[i] = 0;
+  __syncthreads();
+
+  // ---- radix select of the kk-th largest key over the whole cluster ----
+  uint32_t prefix = 0, pmask = 0;
+  uint32_t krem = static_cast<uint32_t>(kk);
+  for (int pass = 0; pass < 4; ++pass) {
+    const int buf = pass & 1;
+    const int shift = 24 - 8 * pass;
+    if (pass >= 2) {
+      // hist[buf] was last read by the cluster before the previous pass's
+      // cluster.sync(); clear it for reuse.
+      for (int i = threadIdx.x; i < 256; i += SEL_THREADS) hist[buf][i] = 0;
+      __syncthreads();
+    }
+    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+      const uint32_t k = keys[i];
+      if ((k & pmask) == prefix) atomicAdd(&hist[buf][(k >> shift) & 255u], 1u);
+    }
+    cluster.sync();
+    if (threadIdx.x < 256) {
+      uint32_t s = 0;
+      for (int rr = 0; rr < C; ++rr) s += cluster.map_shared_rank(&hist[buf][0], rr)[threadIdx.x];
+      tot[threadIdx.x] = s;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l owns digits [248-8l, 255-8l], scanned from the top.
+      const int lane = threadIdx.x;
+      uint32_t lsum = 0;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) lsum += tot[255 - 8 * lane - d];
+      uint32_t incl = lsum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      uint32_t cum = incl - lsum;  // keys with a larger digit than this lane's range
+      if (cum < krem && krem <= incl) {
+#pragma unroll 1
+        for (int d = 0; d < 8; ++d) {
+          const int digit = 255 - 8 * lane - d;
+          const uint32_t c = tot[digit];
+          if (cum + c >= krem) {
+            sel_digit = static_cast<uint32_t>(digit);
+            sel_krem = krem - cum;
+            break;
+          }
+          cum += c;
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= sel_digit << shift;
+    pmask |= 255u << shift;
+    krem = sel_krem;
+    __syncthreads();
+  }
+  const uint32_t T = prefix;    // the kk-th largest key
+  const uint32_t need_eq = krem; // how many keys equal to T are kept (lowest indices)
+
+  // ---- per-CTA counts, exchanged for offsets ----
+  int gt = 0, eq = 0;
+  for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+    const uint32_t k = keys[i];
+    gt += k > T;
+    eq += k == T;
+  }
+  {
+    __shared__ int red[2][SEL_WARPS];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      gt += __shfl_xor_sync(0xffffffffu, gt, o);
+      eq += __shfl_xor_sync(0xffffffffu, eq, o);
+    }
+    if (lane == 0) {
+      red[0][warp] = gt;
+      red[1][warp] = eq;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      long long tg = 0, te = 0;
+      for (int w = 0; w < SEL_WARPS; ++w) {
+        tg += red[0][w];
+        te += red[1][w];
+      }
+      counts[0] = tg;
+      counts[1] = te;
+    }
+  }
+  cluster.sync();
+  long long gt_before = 0, eq_before = 0;
+  for (int rr = 0; rr < crank; ++rr) {
+    const long long* rc = cluster.map_shared_rank(&counts[0], rr);
+    gt_before += rc[0];
+    eq_before += rc[1];
+  }
+  // Keep remote CTAs' shared memory alive until everyone has read it.
+  cluster.sync();
+
+  // ---- ordered compaction ----
+  long long run_gt = gt_before, run_eq = eq_before;
+  for (int base = 0; base < len; base += SEL_THREADS) {
+    const int i = base + threadIdx.x;
+    const bool in = i < len;
+    const uint32_t k = in ? keys[i] : 0u;
+    const bool is_eq = in && (k == T);
+    int tot_eq;
+    const int eq_rank = block_flag_scan(is_eq, warp_sums, &tot_eq);
+    const bool kept_eq = is_eq && (run_eq + eq_rank < static_cast<long long>(need_eq));
+    const bool kept = (in && k > T) || kept_eq;
+    int tot_kept;
+    const int pos = block_flag_scan(kept, warp_sums, &tot_kept);
+    // kept elements before this one over the whole row:
+    //   gt before the tile + kept-equal before the tile + in-tile prefix
+    const long long kept_eq_before = min(run_eq, static_cast<long long>(need_eq));
+    if (in) {
+      if (kept) out_idx[run_gt + kept_eq_before + pos] = lo + i;
+      out_mask[lo + i] = kept ? keep_v : evict_v;
+    }
+    const long long kept_eq_after = min(run_eq + tot_eq, static_cast<long long>(need_eq));
+    run_gt += tot_kept - (kept_eq_after - kept_eq_before);
+    run_eq += tot_eq;
+  }
+}
+
+}  // namespace fe

@@ -1,0 +1,9 @@
+"""B200-native drop-in for the reference's `flash_evict` package.
+
+`prefill`, `evict` and `select_tokens` keep the reference's signatures
+(flash_evict/__init__.py:1-3 of the reference); the compute runs in the
+sm_100a native library bound by `_lib`.
+"""
+from .prefill import prefill, evict, select_tokens
+
+__all__ = ["prefill", "evict", "select_tokens"]

@@ -1,0 +1,133 @@
+/*
+ * flash_evict.h -- C ABI of the B200 (sm_100a) evict() prefill path.
+ *
+ * The reference (anishesg/flash-evict-prefill) is a Python package whose hot
+ * path is one Triton kernel plus PyTorch selection ops.  Each entry point below
+ * replaces one piece of that path; the Python package `flash_evict` (same
+ * module path and signatures as the reference) binds them with ctypes.
+ *
+ * Conventions
+ *  - All pointers are device pointers unless stated otherwise; sizes are
+ *    element counts; strides are in elements.
+ *  - Q is [batch, q_heads, tokens, channels], K and V are
+ *    [batch, kv_heads, tokens, channels], each with arbitrary strides as long
+ *    as the channel stride is 1, the other strides are multiples of 8 elements
+ *    (16 bytes) and the base pointer is 16-byte aligned (the TMA rules).
+ *  - dtype: FE_DTYPE_F16 or FE_DTYPE_BF16.  Q, K, V and the output share it.
+ *  - `stream` is a cudaStream_t passed as void*; every launch is asynchronous
+ *    on it and no entry point synchronizes the host.
+ *  - Return value: FE_STATUS_OK or an error code; fe_last_error() gives the
+ *    message for the calling thread.  Device-side watchdog timeouts surface
+ *    through fe_device_status().
+ *  - A "query block" is FE_QUERY_BLOCK consecutive query rows.  Passing
+ *    query_blocks == NULL processes all rows; otherwise only the listed block
+ *    indices (device int32 array) are processed, which is how a rank of a
+ *    query-sharded job restricts the work to its own rows.
+ */
+#ifndef FLASH_EVICT_B200_H
+#define FLASH_EVICT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FE_API __attribute__((visibility("default")))
+#else
+#define FE_API
+#endif
+
+#define FE_STATUS_OK 0
+#define FE_STATUS_INVALID 1     /* bad argument (shape, stride, value)          */
+#define FE_STATUS_UNSUPPORTED 2 /* valid request outside what the kernels do    */
+#define FE_STATUS_CUDA 3        /* a CUDA runtime/driver call failed            */
+#define FE_STATUS_TIMEOUT 4     /* a device wait exceeded the watchdog limit    */
+
+#define FE_DTYPE_F16 0
+#define FE_DTYPE_BF16 1
+
+#define FE_QUERY_BLOCK 256
+
+/* Attention forward (traversal 1).
+ * Replaces the first KV traversal of `_prefill` (flash_evict/prefill.py:23-60)
+ * and the output allocation/launch of `prefill` (flash_evict/prefill.py:102-137).
+ * Writes out = softmax(scale * Q K^T [causal]) V as a contiguous
+ * [batch, q_heads, tokens, channels] tensor of `dtype`, and the final softmax
+ * statistics of each query row to row_stats[(b*q_heads+h)*tokens+q] =
+ * {m, l} (FP32; m in log2 units of scale*log2(e)*logit, l the row sum of
+ * exp2(logit*scale*log2e - m)).  Deterministic: the same inputs give the same
+ * bits whether or not scores are computed afterwards. */
+FE_API int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                     const void* v, const int64_t* v_strides, void* out, float* row_stats, int64_t batch,
+                     int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype,
+                     int causal, float scale, const int32_t* query_blocks, int64_t num_query_blocks,
+                     void* stream);
+
+/* Exact importance by replay (traversal 2), one store per KV token.
+ * Replaces the replay loop and atomics of `_prefill`
+ * (flash_evict/prefill.py:61-83) and the zero-fill of the score buffer
+ * (flash_evict/prefill.py:129):
+ *   importance[b,hkv,k] = ||V[b,hkv,k]||_1 (if value_weighted)
+ *       * sum_{g, q} w_q * softmax(QK^T)[b, hkv*G+g, q, k]
+ *   w_q = exp(recency_decay * (q - (tokens-1))) * [q >= tokens - W],
+ *   W = min(tokens, observation_window or tokens).
+ * row_stats must come from fe_attention_fwd on the same inputs.  Each output
+ * element is written exactly once in a fixed order (no atomics, bitwise
+ * reproducible).  Rows whose FP32 weight underflows (< 2^-126) are skipped.
+ * With query_blocks != NULL the sum runs over the listed query blocks only
+ * (a partial sum, to be all-reduced across ranks). */
+FE_API int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                     const void* v, const int64_t* v_strides, const float* row_stats, float* importance,
+                     int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels,
+                     int dtype, int causal, float scale, float recency_decay, int64_t observation_window,
+                     int value_weighted, const int32_t* query_blocks, int64_t num_query_blocks, void* stream);
+
+/* Token selection.  Replaces `select_tokens` (flash_evict/prefill.py:140-170).
+ * importance: contiguous FP32 [rows, tokens].  For each row: the past region
+ * is the first tokens-recent scores; if pool_kernel > 1 and budget > recent it
+ * is average-pooled (stride 1, zero padding pool_kernel/2, divisor
+ * pool_kernel); the budget-recent largest pooled scores are kept (ties: larger
+ * value first, then lower index; NaN counts as largest) together with the last
+ * `recent` tokens.  indices: int64 [rows, budget], ascending.  mask: uint8
+ * [rows, tokens]; with mask_evict != 0 an element is 1 when the token is
+ * evicted (the reference's ~keep), else 1 when kept. */
+FE_API int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
+                     int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, void* stream);
+
+/* The whole evict() path in one call (attention, replay, selection).
+ * Replaces `evict` (flash_evict/prefill.py:173-180).  row_stats is caller
+ * workspace of 2*batch*q_heads*tokens floats.  mask is the eviction mask
+ * (1 = evict). */
+FE_API int fe_evict(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+             const int64_t* v_strides, void* out, float* importance, int64_t* indices, uint8_t* mask,
+             float* row_stats, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens,
+             int64_t channels, int dtype, int causal, float scale, float recency_decay,
+             int64_t observation_window, int value_weighted, int64_t budget, int64_t recent,
+             int64_t pool_kernel, void* stream);
+
+/* Read (and optionally clear) the device status word of `device`: the largest
+ * FE_STATUS_* code any kernel raised since the last clear.  Synchronizes that
+ * device. */
+FE_API int fe_device_status(int device, int clear, int* status_out);
+
+/* Watchdog limit for every device-side wait, in nanoseconds (default 2e9). */
+FE_API void fe_set_watchdog_ns(int64_t ns);
+
+/* Launch a kernel whose bounded wait can never be satisfied, with the given
+ * limit; it raises FE_STATUS_TIMEOUT and returns cleanly.  Used by tests to
+ * exercise the timeout path without hanging a GPU. */
+FE_API int fe_watchdog_selftest(int64_t timeout_ns, void* stream);
+
+/* Message describing the last error returned on the calling thread. */
+FE_API const char* fe_last_error(void);
+
+/* ABI version of this library. */
+FE_API int fe_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_EVICT_B200_H */
