@@ -1,0 +1,369 @@
+"""Benchmark of the evict() prefill path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c2|c5]
+
+Headline (BASELINE.json metric, configs[2] = "c3"): evict() for B1 Hq28 Hkv4
+N32768 D128 fp16 causal, observation_window 128, pool_kernel 5, budget 2048,
+1% of K rows x8.  value = (attention + replay FLOPs) / device time per step,
+with inputs resident in HBM (inputs are larger than the 126 MB L2, so no
+flush is needed).  One step = one evict() call = 3 kernel launches.
+
+Under torchrun (N > 1) every rank processes its own batch element of the same
+shape (weak scaling, no collective on the data path); value is the FLOPs of
+all ranks divided by the slowest rank's time.  `--workload c4` runs the
+131K-token query-sharded configuration with one NCCL all-reduce of the scores
+(strong scaling) through flash_evict.distributed.
+
+--impl reference times the CPU restatement of the reference's path (oracle/,
+numpy; the reference itself is a Python/Triton package that cannot run on the
+host cores) on a bounded sample of the same workload, rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "flash-evict-prefill_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "evict() prefill TFLOP/s (% tcgen05 peak) at N=32K; overhead vs attention-only"
+
+WORKLOADS = {
+    # name: (B, Hq, Hkv, N, D, dtype, causal, evict kwargs, budget, description)
+    "c3": dict(b=1, hq=28, hkv=4, n=32768, d=128, dtype=torch.float16, causal=True, budget=2048,
+               kw=dict(observation_window=128, pool_kernel=5), sinks=True, qscale=1.0,
+               desc="Qwen-style GQA 7:1 B1 Hq28 Hkv4 N32768 D128 fp16 causal, window 128, pool 5, budget 2048, "
+                    "1% of K rows x8"),
+    "c2": dict(b=1, hq=32, hkv=8, n=8192, d=128, dtype=torch.bfloat16, causal=True, budget=1024,
+               kw=dict(recency_decay=0.1, reserved_recent=64), sinks=False, qscale=128 ** -0.25,
+               desc="Llama-3-8B-shaped B1 Hq32 Hkv8 N8192 D128 bf16 causal, decay 0.1, reserved 64, budget 1024"),
+    "c5": dict(b=8, hq=32, hkv=32, n=4096, d=128, dtype=torch.float16, causal=False, budget=410,
+               kw=dict(value_weighted=False), sinks=False, qscale=30.0, transposed=True, zero_v=0.05,
+               desc="Batched MHA B8 Hq=Hkv=32 N4096 D128 fp16 noncausal, [B,N,H,D] strides, q x30, 5% zero V "
+                    "rows, H2O, budget 410"),
+}
+
+# DRAM traffic of one attention-forward launch at c3, from the ncu capture
+# summarised in profiles/ (None until captured).
+TRAFFIC_PER_FWD_LAUNCH = None
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return p.get("bf16_tflops"), p.get("bf16_tflops_sustained"), p.get("hbm_gbs"), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def make_inputs(w, seed, device):
+    g = torch.Generator().manual_seed(seed)
+    b, hq, hkv, n, d = w["b"], w["hq"], w["hkv"], w["n"], w["d"]
+    if w.get("transposed"):
+        q = torch.randn((b, n, hq, d), generator=g) * w["qscale"]
+        k = torch.randn((b, n, hkv, d), generator=g)
+        v = torch.randn((b, n, hkv, d), generator=g)
+        if w.get("zero_v"):
+            zero = torch.randperm(n, generator=g)[: int(n * w["zero_v"])]
+            v[:, zero] = 0
+        q, k, v = (t.to(w["dtype"]).to(device).transpose(1, 2) for t in (q, k, v))
+        return q, k, v
+    q = torch.randn((b, hq, n, d), generator=g) * w["qscale"]
+    k = torch.randn((b, hkv, n, d), generator=g) * (w["qscale"] if w["qscale"] < 1 else 1.0)
+    v = torch.randn((b, hkv, n, d), generator=g)
+    if w["sinks"]:
+        sink = torch.randperm(n, generator=g)[: n // 100]
+        k[:, :, sink] *= 8
+    return tuple(t.to(w["dtype"]).to(device) for t in (q, k, v))
+
+
+def flops(w):
+    from oracle import restate as O
+    b, hq, n, d = w["b"], w["hq"], w["n"], w["d"]
+    f_attn = O.attention_flops(b, hq, n, d, w["causal"])
+    kw = w["kw"]
+    rows_kept = O.scored_rows(n, kw.get("recency_decay", 0.0), kw.get("observation_window", 0), True)
+    rows_all = O.scored_rows(n, kw.get("recency_decay", 0.0), kw.get("observation_window", 0), False)
+    f_rep = O.replay_flops(b, hq, n, d, w["causal"], rows_kept)
+    f_rep_all = O.replay_flops(b, hq, n, d, w["causal"], rows_all)
+    return f_attn, f_rep, f_rep_all
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        busy = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_oracle_sample(w, q, k, v, seconds=12.0):
+    """Time the numpy restatement on a bounded sample of the workload: the
+    output rows of one query head, taken from the end of the sequence (the
+    longest rows), chunk by chunk until ~`seconds` of CPU work.  Returns
+    (TFLOP/s, description, threads)."""
+    from oracle import restate as O
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((p.get("num_threads", 1) for p in threadpool_info()), default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count()
+    n, d = w["n"], w["d"]
+    qh = q[0:1, 0:1].float().cpu().numpy()
+    kh = k[0:1, 0:1].float().cpu().numpy()
+    vh = v[0:1, 0:1].float().cpu().numpy()
+    done_flops, rows_done, t0 = 0, 0, time.perf_counter()
+    chunk = 256
+    hi = n
+    while time.perf_counter() - t0 < seconds and hi > 0:
+        lo = max(0, hi - chunk)
+        rows = np.arange(lo, hi)
+        O.chunked(qh, kh, vh, causal=w["causal"], out_rows=rows, observation_window=1, chunk=chunk,
+                  dtype=np.float32, value_weighted=w["kw"].get("value_weighted", True))
+        keys = (rows + 1).sum() if w["causal"] else len(rows) * n
+        done_flops += 4 * d * int(keys)
+        rows_done += len(rows)
+        hi = lo
+    dt = time.perf_counter() - t0
+    desc = (f"oracle/restate.py chunked float32 numpy: {rows_done} query rows (from the end) of 1 head of "
+            f"{w['hq']}, {dt:.1f} s, scaled by FLOPs")
+    return done_flops / dt / 1e12, desc, threads
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    q, k, v = make_inputs(w, 0, "cpu")
+    vals = []
+    desc, threads = "", 1
+    for i in range(args.warmup + args.steps):
+        val, desc, threads = cpu_oracle_sample(w, q, k, v, seconds=4.0 if i < args.warmup else 8.0)
+        if i >= args.warmup:
+            vals.append(val)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload + ": " + w["desc"]},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, w):
+    import torch.distributed as dist
+    from flash_evict import _lib, evict, prefill
+    from flash_evict.prefill import _evict_impl
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    q, k, v = make_inputs(w, 1000 + rank, dev)
+    kw = dict(w["kw"])
+    budget = w["budget"]
+    recent = kw.pop("reserved_recent", 0)
+    pool = kw.pop("pool_kernel", 1)
+    kw["causal"] = w["causal"]
+    f_attn, f_rep, f_rep_all = flops(w)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---------------- device-resident timed region: value + roofline -------
+    n_ev = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
+    slot = {"i": -1}
+    stages = {"start": 0, "attention": 1, "replay": 2, "select": 3}
+
+    def marks(stage):
+        if slot["i"] >= 0:
+            ev[slot["i"]][stages[stage]].record(stream)
+
+    for _ in range(args.warmup):
+        _evict_impl(q, k, v, budget, 0, recent, pool, None, kw)
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        slot["i"] = i
+        _evict_impl(q, k, v, budget, 0, recent, pool, marks, kw)
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    slot["i"] = -1
+    total_ms = max_over_ranks(t0.elapsed_time(t1))
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    rep_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    sel_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    ms_per_step = total_ms / args.steps
+    step_flops = f_attn + f_rep
+    value = step_flops * world / (ms_per_step * 1e-3) / 1e12
+
+    # ---------------- attention-only (same forward kernel, no replay) -------
+    prefill_kw = dict(w["kw"])
+    prefill_kw.pop("reserved_recent", None)
+    prefill_kw.pop("pool_kernel", None)
+    for _ in range(2):
+        prefill(q, k, v, causal=w["causal"], score=False)
+    barrier()
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(args.steps):
+        prefill(q, k, v, causal=w["causal"], score=False)
+    a1.record(stream)
+    barrier()
+    attn_only_ms = max_over_ranks(a0.elapsed_time(a1)) / args.steps
+
+    # ---------------- end to end: host buffers, copies inside the region ---
+    hq_, hk_, hv_ = (t.detach().cpu().pin_memory() for t in (q, k, v))
+    dq, dk, dv = (torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (hq_, hk_, hv_))
+    if w.get("transposed"):
+        dq, dk, dv = (t for t in (dq, dk, dv))
+    h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_))
+    outs = None
+    host_out = None
+    e2e_steps = max(2, min(args.steps, 10))
+    for it in range(e2e_steps + 1):
+        if it == 1:
+            barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        dq.copy_(hq_, non_blocking=True)
+        dk.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        outs = evict(dq, dk, dv, budget, reserved_recent=recent, pool_kernel=pool, **kw)
+        if host_out is None:
+            host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+        for h_, d_ in zip(host_out, outs):
+            h_.copy_(d_, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    e2e_value = step_flops * world / (e2e_ms * 1e-3) / 1e12
+
+    status = _lib.device_status(local)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    burst, sustained, hbm, src = peaks()
+    achieved = f_attn / (fwd_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16" if w["dtype"] == torch.float16 else "bf16", "data": "synthetic",
+        "config": {"workload": args.workload + ": " + w["desc"], "global_batch": w["b"] * world,
+                   "seq_len": w["n"], "parallelism": f"replicas x{world} (batch element per GPU, no collective)"
+                   if world > 1 else "single GPU", "l2": "inputs larger than L2 (no flush)",
+                   "flops_per_step": step_flops, "attention_flops": f_attn, "replay_flops": f_rep,
+                   "replay_flops_without_underflow_skip": f_rep_all},
+        "overhead_vs_attention_only": ms_per_step / attn_only_ms,
+        "attention_only_ms": attn_only_ms,
+        "kernel_ms": {"attention": fwd_ms, "replay": rep_ms, "select": sel_ms},
+        "pct_of_peak": {"value_vs_sustained": value / world / sustained, "value_vs_burst": value / world / burst},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                     "frac": achieved / sustained, "traffic": TRAFFIC_PER_FWD_LAUNCH,
+                     "kernel": "fe_fwd_kernel (attention forward)",
+                     "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a multi-second loop)"},
+        "clocks": clk,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": 3 * args.steps,
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        val, desc, threads = cpu_oracle_sample(w, q, k, v, seconds=10.0)
+        line["cpu_baseline"] = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -116,16 +116,28 @@ int check_shapes(int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int d
   return FE_STATUS_OK;
 }
 
+// Opt a kernel into `bytes` of dynamic shared memory, once per (kernel,
+// device).  Keyed by the kernel's address: every template instantiation is a
+// distinct kernel even when the function types coincide.
 template <typename K>
 int set_smem(K kernel, int bytes) {
-  // One attribute call per kernel instantiation and device.
-  static int done[64] = {0};
+  struct Entry {
+    const void* fn;
+    int dev;
+    int bytes;
+  };
+  static Entry cache[256];
+  static int used = 0;
+  static std::mutex mu;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && done[dev] >= bytes) return FE_STATUS_OK;
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == fn && cache[i].dev == dev && cache[i].bytes >= bytes) return FE_STATUS_OK;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-  if (dev < 64) done[dev] = bytes;
+  if (used < 256) cache[used++] = Entry{fn, dev, bytes};
   return FE_STATUS_OK;
 }
 

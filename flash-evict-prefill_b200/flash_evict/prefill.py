@@ -193,9 +193,53 @@ def select_tokens(importance, budget, *, recent=0, reserved_recent=None, pool_ke
 
 def evict(q, k, v, budget, *, recent=0, reserved_recent=None, pool_kernel=1, **kwargs):
     """Return output, importance, kept indices, and bool eviction mask (True=evict)."""
+    return _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, None, kwargs)
+
+
+def _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, marks, kwargs):
+    """Body of `evict` (reference prefill.py:173-180): prefill then selection,
+    with the eviction mask written directly by the selection kernel.
+    `marks`, when given, is called with a stage name before the first launch
+    and after each launch (bench.py places CUDA events there)."""
     if kwargs.get("score") is False:
         raise ValueError("evict requires importance scoring")
-    output, importance = prefill(q, k, v, **kwargs)
-    recent = _check_select_args(importance.shape[-1], budget, recent, reserved_recent, pool_kernel)
-    indices, eviction_mask = _select(importance, budget, recent, pool_kernel, evict_mask=True)
-    return output, importance, indices, eviction_mask
+    kwargs = dict(kwargs)
+    kwargs.pop("score", None)
+    causal = kwargs.pop("causal", True)
+    value_weighted = kwargs.pop("value_weighted", True)
+    recency_decay = kwargs.pop("recency_decay", 0.)
+    observation_window = kwargs.pop("observation_window", 0)
+    block_q = kwargs.pop("block_q", 32)
+    block_k = kwargs.pop("block_k", 64)
+    scale = kwargs.pop("scale", None)
+    if kwargs:
+        raise TypeError(f"prefill() got unexpected keyword arguments {sorted(kwargs)}")
+    _validate(q, k, v)
+    recency_decay, scale = _check_prefill_args(recency_decay, observation_window, block_q, block_k, scale,
+                                               q.shape[-1])
+    b, h, n, d = q.shape
+    hk = k.shape[1]
+    recent = _check_select_args(n, budget, recent, reserved_recent, pool_kernel)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    row_stats = torch.empty((b, h, n, 2), dtype=torch.float32, device=q.device)
+    importance = torch.empty((b, hk, n), dtype=torch.float32, device=q.device)
+    indices = torch.empty((b, hk, budget), dtype=torch.int64, device=q.device)
+    eviction_mask = torch.empty((b, hk, n), dtype=torch.bool, device=q.device)
+    qv, kv, vv = _tma_view(q), _tma_view(k), _tma_view(v)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        if marks:
+            marks("start")
+        _attention(qv, kv, vv, out, row_stats, causal, scale)
+        if marks:
+            marks("attention")
+        _replay(qv, kv, vv, row_stats, importance, causal, scale, recency_decay, observation_window,
+                value_weighted)
+        if marks:
+            marks("replay")
+        _lib.check(lib.fe_select_tokens(
+            importance.data_ptr(), b * hk, n, budget, recent, pool_kernel, indices.data_ptr(),
+            eviction_mask.data_ptr(), 1, _stream(q.device)))
+        if marks:
+            marks("select")
+    return out, importance, indices, eviction_mask

@@ -76,14 +76,17 @@ def materialized(q, k, v, *, causal=True, value_weighted=True, scale=None, recen
 
 
 def chunked(q, k, v, *, causal=True, value_weighted=True, scale=None, recency_decay=0.0,
-            observation_window=0, out_rows=None, chunk=256, dtype=np.float64, weight_floor=0.0):
+            observation_window=0, out_rows=None, chunk=256, dtype=np.float64, weight_floor=0.0,
+            score_rows=None):
     """Query-chunked restatement of reference.py:5-25 for long sequences.
 
     Row softmax is exact per query chunk (all keys at once); the weighted
     column sums accumulate in float64.  out_rows: None -> outputs for every
     row; an index array -> outputs only for those rows (others left NaN);
     an empty list -> no outputs.  Rows whose weight is <= weight_floor are
-    not visited for the importance.
+    not visited for the importance.  score_rows restricts the importance
+    sum to those query rows (a partial sum, as one rank of a query-sharded
+    job computes it).
     Returns (out [B,Hq,N,D] float32, mass [B,Hkv,N] float32).
     """
     q, k, v = (_as_np(t) for t in (q, k, v))
@@ -92,6 +95,10 @@ def chunked(q, k, v, *, causal=True, value_weighted=True, scale=None, recency_de
     groups = hq // hkv
     sc = d ** -0.5 if scale is None else scale
     w = recency_weights(n, recency_decay, observation_window, np.float64)
+    if score_rows is not None:
+        keep = np.zeros(n, dtype=bool)
+        keep[np.asarray(score_rows, dtype=np.int64)] = True
+        w = np.where(keep, w, 0.0)
     scored = np.nonzero(w > weight_floor)[0]
     if out_rows is None:
         want_out = np.arange(n)

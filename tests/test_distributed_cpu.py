@@ -1,0 +1,138 @@
+"""Host logic of the multi-GPU layer on CPU ranks (gloo, world size 2).
+
+The query-sharded pipeline (flash_evict.distributed._query_sharded) runs
+with the oracle standing in for the per-rank CUDA compute, so the partition,
+the all-reduce of partial scores, the row all-gather and the per-rank
+selection are checked without a GPU.  A rank that fails before the
+collective must make its peer's collective fail on the process-group
+timeout, not hang.
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from flash_evict.distributed import _query_sharded, head_unit_plan, query_block_plan, _block_cost, BLOCK
+from oracle import restate as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+@pytest.mark.parametrize("n,world,causal", [(131072, 8, True), (131072, 3, True), (32768, 2, True),
+                                            (4096, 4, False), (300, 2, True), (100, 4, True)])
+def test_query_block_plan_partitions_and_balances(n, world, causal):
+    plan = query_block_plan(n, world, causal)
+    nblk = (n + BLOCK - 1) // BLOCK
+    flat = sorted(b for p in plan for b in p)
+    assert flat == list(range(nblk))
+    costs = [sum(_block_cost(b, n, causal) for b in p) for p in plan]
+    max_block = max(_block_cost(b, n, causal) for b in range(nblk))
+    assert max(costs) - min(costs) <= max_block
+    for p in plan:
+        c = [_block_cost(b, n, causal) for b in p]
+        assert c == sorted(c, reverse=True)
+
+
+@pytest.mark.parametrize("batch,heads,world", [(8, 32, 8), (8, 32, 3), (1, 8, 8), (2, 3, 4)])
+def test_head_unit_plan_covers_units(batch, heads, world):
+    plan = head_unit_plan(batch, heads, world)
+    units = [(b, h) for runs in plan for (b, h0, h1) in runs for h in range(h0, h1)]
+    assert sorted(units) == [(b, h) for b in range(batch) for h in range(heads)]
+    sizes = [sum(h1 - h0 for _, h0, h1 in runs) for runs in plan]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def _oracle_partial(q, k, v, blocks, causal, scale, decay, window, weighted):
+    n = q.shape[2]
+    rows = np.concatenate([np.arange(b * BLOCK, min(n, (b + 1) * BLOCK)) for b in blocks]) if blocks else \
+        np.zeros(0, dtype=np.int64)
+    out, mass = O.chunked(q, k, v, causal=causal, value_weighted=weighted, scale=scale, recency_decay=decay,
+                          observation_window=window, out_rows=rows, score_rows=rows)
+    if out is None:
+        out = np.zeros(q.shape, dtype=np.float32)
+    out = np.nan_to_num(out, nan=0.0)
+    return torch.from_numpy(out), torch.from_numpy(mass)
+
+
+def _oracle_select(importance, budget, recent, pool):
+    idx, keep = O.select_tokens(importance.numpy(), budget, reserved_recent=recent, pool_kernel=pool)
+    return torch.from_numpy(idx), torch.from_numpy(~keep)
+
+
+def _worker(rank, world, port, result_dir, mode):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    g = torch.Generator().manual_seed(0)
+    n, h, hk, d = 700, 4, 2, 32
+    q = torch.randn(1, h, n, d, generator=g)
+    k = torch.randn(1, hk, n, d, generator=g)
+    v = torch.randn(1, hk, n, d, generator=g)
+    try:
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("injected failure before the score all-reduce")
+        out, imp, idx, mask, blocks = _query_sharded(
+            q, k, v, 64, 8, 5, True, d ** -0.5, 0.01, 0, True, True, None, _oracle_partial, _oracle_select)
+        np.savez(os.path.join(result_dir, f"r{rank}.npz"), out=out.numpy(), imp=imp.numpy(), idx=idx.numpy(),
+                 mask=mask.numpy(), blocks=np.array(blocks))
+    except Exception as e:  # noqa: BLE001
+        with open(os.path.join(result_dir, f"r{rank}.err"), "w") as f:
+            f.write(type(e).__name__ + ": " + str(e))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+def _spawn(mode, tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(60)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+
+
+def test_query_sharded_pipeline_gloo(tmp_path):
+    _spawn("ok", tmp_path)
+    r0 = np.load(tmp_path / "r0.npz")
+    r1 = np.load(tmp_path / "r1.npz")
+    g = torch.Generator().manual_seed(0)
+    n, h, hk, d = 700, 4, 2, 32
+    q = torch.randn(1, h, n, d, generator=g)
+    k = torch.randn(1, hk, n, d, generator=g)
+    v = torch.randn(1, hk, n, d, generator=g)
+    ref_out, ref_imp = O.chunked(q, k, v, recency_decay=0.01)
+    np.testing.assert_allclose(r0["imp"], ref_imp, rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(r0["imp"], r1["imp"])
+    np.testing.assert_allclose(r0["out"], ref_out, rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(r0["idx"], r1["idx"])
+    ref_idx, ref_keep = O.select_tokens(ref_imp, 64, reserved_recent=8, pool_kernel=5)
+    np.testing.assert_array_equal(r0["idx"], ref_idx)
+    assert sorted(np.r_[r0["blocks"], r1["blocks"]].tolist()) == list(range((n + BLOCK - 1) // BLOCK))
+
+
+def test_failed_rank_surfaces_as_error_not_hang(tmp_path):
+    _spawn("fail", tmp_path)
+    assert (tmp_path / "r1.err").exists()
+    err0 = tmp_path / "r0.err"
+    assert err0.exists(), "surviving rank should see its collective fail"
