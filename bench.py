@@ -241,6 +241,14 @@ def run_ours(args, w):
 
     for _ in range(args.warmup):
         _evict_impl(q, k, v, budget, 0, recent, pool, None, kw)
+    if args.profile:
+        # Short run for ncu: warm-up plus K evict() steps, nothing else.
+        for _ in range(args.steps):
+            _evict_impl(q, k, v, budget, 0, recent, pool, None, kw)
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_run": args.workload, "steps": args.steps, "warmup": args.warmup,
+                          "launches_per_step": 3, "device_status": _lib.device_status(local)}), flush=True)
+        return
     clocks = Clocks(local)
     barrier()
     clocks.start()
@@ -351,11 +359,12 @@ def run_ours(args, w):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="warm-up + K evict() steps only (for ncu)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     w = WORKLOADS[args.workload]
