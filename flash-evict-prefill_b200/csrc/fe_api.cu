@@ -403,3 +403,74 @@ int fe_watchdog_selftest(int64_t timeout_ns, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free evict().
+//
+// Some callers cannot allocate device memory at the point where they run
+// eviction: code inside a custom memory pool that owns all of the GPU's
+// memory, engines that reserve every byte up front and forbid cudaMalloc on
+// the serving path, or plain C/FFI hosts that have no allocator of their own.
+// fe_evict needs one piece of scratch besides the caller's inputs and outputs:
+// the per-row softmax statistics {m, l} written by the attention kernel and
+// read back by the replay kernel.  This variant keeps that scratch in a
+// fixed-size array that lives in the library itself.
+//
+// The array is reserved on every GPU that loads this library and stays there
+// until the process exits (32 MiB).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = int64_t(1) << 22;  // batch*q_heads*tokens rows of {m, l}
+
+static __device__ __align__(256) float2 fe_noalloc_row_stats[kNoAllocMaxRows];
+
+// Device address of fe_noalloc_row_stats on each device, looked up once.
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= 64) return fail(FE_STATUS_UNSUPPORTED, "fe_evict_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    // The caller's device is current here (bind_device); the symbol's host
+    // name is only a stand-in, so ask the runtime for its device address.
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, fe_noalloc_row_stats);
+    if (e != cudaSuccess) return cuda_fail(e, "fe_evict_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<float*>(g_noalloc_ptr[dev]);
+  return FE_STATUS_OK;
+}
+
+}  // namespace
+
+extern "C" int fe_evict_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                const void* v, const int64_t* v_strides, void* out, float* importance,
+                                int64_t* indices, uint8_t* mask, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                int64_t tokens, int64_t channels, int dtype, int causal, float scale,
+                                float recency_decay, int64_t observation_window, int value_weighted, int64_t budget,
+                                int64_t recent, int64_t pool_kernel, void* stream) {
+  g_err[0] = 0;
+  if (batch < 1 || q_heads < 1 || tokens < 1)
+    return fail(FE_STATUS_INVALID, "fe_evict_noalloc: empty shape");
+  if (batch > kNoAllocMaxRows || q_heads > kNoAllocMaxRows || tokens > kNoAllocMaxRows ||
+      batch * q_heads > kNoAllocMaxRows || batch * q_heads * tokens > kNoAllocMaxRows)
+    return fail(FE_STATUS_UNSUPPORTED,
+                "fe_evict_noalloc: batch*q_heads*tokens = %lld exceeds the built-in scratch capacity of %lld rows; "
+                "use fe_evict with a caller-provided workspace",
+                (long long)(batch * q_heads * tokens), (long long)kNoAllocMaxRows);
+  if (!q) return fail(FE_STATUS_INVALID, "null pointer");
+  int dev = 0;
+  int rc = bind_device(q, &dev);
+  if (rc) return rc;
+  float* scratch = nullptr;
+  rc = noalloc_scratch(dev, &scratch);
+  if (rc) return rc;
+  // Every row the replay reads is written by the attention kernel earlier on
+  // the same stream, so the scratch needs no clearing between calls.
+  return fe_evict(q, q_strides, k, k_strides, v, v_strides, out, importance, indices, mask, scratch, batch, q_heads,
+                  kv_heads, tokens, channels, dtype, causal, scale, recency_decay, observation_window, value_weighted,
+                  budget, recent, pool_kernel, stream);
+}

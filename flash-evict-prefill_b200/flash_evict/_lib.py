@@ -43,6 +43,8 @@ SIGNATURES = {
     "fe_select_tokens": (_INT, [_VP, _I64, _I64, _I64, _I64, _I64, _VP, _VP, _INT, _VP]),
     "fe_evict": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64,
                         _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
+    "fe_evict_noalloc": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _I64, _I64, _I64,
+                                _I64, _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
     "fe_device_status": (_INT, [_INT, _INT, ctypes.POINTER(_INT)]),
     "fe_set_watchdog_ns": (None, [_I64]),
     "fe_watchdog_selftest": (_INT, [_I64, _VP]),

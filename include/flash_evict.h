@@ -107,6 +107,28 @@ FE_API int fe_evict(const void* q, const int64_t* q_strides, const void* k, cons
              int64_t observation_window, int value_weighted, int64_t budget, int64_t recent,
              int64_t pool_kernel, void* stream);
 
+/* evict() without any device allocation: like fe_evict, but the row-statistics
+ * scratch lives in a fixed array inside this library instead of a
+ * caller-provided workspace.  No counterpart in the reference (which always
+ * allocates through PyTorch); it exists for callers that cannot allocate
+ * device memory when they evict -- custom pools that own all GPU memory,
+ * engines that forbid cudaMalloc on the serving path, plain C/FFI hosts.
+ *  - Limit: batch*q_heads*tokens <= 4194304 (the array is 32 MiB and is
+ *    reserved on every GPU that loads the library until process exit);
+ *    larger requests return FE_STATUS_UNSUPPORTED with a message.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - All calls on a device share the one array: calls that can overlap on the
+ *    GPU (different streams, no ordering between them) race on it.  Nothing
+ *    in it has to start zeroed; each call writes what it later reads.
+ *  - Calls no cudaMalloc, cudaFree or allocating library routine. */
+FE_API int fe_evict_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                            const void* v, const int64_t* v_strides, void* out, float* importance,
+                            int64_t* indices, uint8_t* mask, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                            int64_t tokens, int64_t channels, int dtype, int causal, float scale,
+                            float recency_decay, int64_t observation_window, int value_weighted, int64_t budget,
+                            int64_t recent, int64_t pool_kernel, void* stream);
+
 /* Read (and optionally clear) the device status word of `device`: the largest
  * FE_STATUS_* code any kernel raised since the last clear.  Synchronizes that
  * device. */
