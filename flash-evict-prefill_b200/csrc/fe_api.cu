@@ -148,6 +148,19 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   auto kern = fe::fe_fwd_kernel<BF16, DP>;
   int rc = set_smem(kern, C::SMEM);
   if (rc) return rc;
+  // The kernel moves registers between its warpgroups (setmaxnreg); that is
+  // only safe if the launch allocation covers the split.  Refuse otherwise.
+  static int checked_regs[2][2] = {{0, 0}, {0, 0}};
+  int& regs = checked_regs[BF16 ? 1 : 0][DP == 64 ? 0 : 1];
+  if (regs == 0) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+    regs = fa.numRegs;
+  }
+  if (regs < fe::FWD_REGS_NEEDED)
+    return fail(FE_STATUS_UNSUPPORTED, "attention kernel compiled with %d registers/thread, needs %d", regs,
+                fe::FWD_REGS_NEEDED);
   kern<<<dim3((unsigned)items), dim3(C::THREADS), C::SMEM, stream>>>(tq, tk, tv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
@@ -181,11 +194,34 @@ __global__ void fe_watchdog_kernel(uint64_t timeout_ns) {
   __syncthreads();
 }
 
+__global__ void fe_exp2_selftest_kernel(const float* in, float* poly, float* mufu, int64_t n) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) {
+    poly[i] = fe::exp2_poly(in[i]);
+    mufu[i] = fe::ex2_approx(in[i]);
+  }
+}
+
 }  // namespace
 
 extern "C" {
 
 int fe_abi_version(void) { return 1; }
+
+int fe_selftest_exp2(const float* in, float* out_poly, float* out_mufu, int64_t n, void* stream) {
+  g_err[0] = 0;
+  if (n < 0 || (n > 0 && (!in || !out_poly || !out_mufu))) return fail(FE_STATUS_INVALID, "bad arguments");
+  if (n == 0) return FE_STATUS_OK;
+  int rc = bind_device(in, nullptr);
+  if (rc) return rc;
+  const int64_t blocks = (n + 255) / 256;
+  if (blocks > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "n too large");
+  fe_exp2_selftest_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(in, out_poly, out_mufu,
+                                                                                              n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "exp2 self-test launch");
+  return FE_STATUS_OK;
+}
 
 const char* fe_last_error(void) { return g_err; }
 

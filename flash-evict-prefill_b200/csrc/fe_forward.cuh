@@ -8,11 +8,15 @@
 // online pass.
 //
 // CTA work unit: one query block = two 128-row query tiles (Q0, Q1) of one
-// query head.  KV tiles are 128 keys.  Roles (320 threads):
+// query head.  KV tiles are 128 keys.  Roles (384 threads, 3 warpgroups):
 //   warps 0-3  softmax for Q0 (thread = TMEM lane = query row)
 //   warps 4-7  softmax for Q1
 //   warp  8    TMA producer (Q once, K/V through a STAGES-deep ring)
 //   warp  9    tcgen05 issuer (one thread) and TMEM owner
+//   warps 10-11 idle
+// Registers: launched at 168/thread; the producer warpgroup drops to
+// FWD_REGS_LOW and the softmax warpgroups rise to FWD_REGS_HIGH
+// (2*128*216 + 128*64 = 63488 <= 384*168 = 64512).
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+DP), O1 after.
 // P (16-bit) overwrites the first 64 columns of its S tile and feeds the PV
 // MMA straight from TMEM (A operand in TMEM, V as an MN-major B operand).
@@ -23,6 +27,14 @@
 // too and O_t may be rescaled in place.  The O rescale is lazy: the max used
 // for exponentiation only moves when the true max exceeds it by more than
 // 2^8, which keeps P <= 256 and makes rescales rare.
+//
+// The two softmax warpgroups take turns for their exponentials (a token
+// passed through the turn[] mbarriers): while one warpgroup exponentiates,
+// the tensor pipe runs the other tile's PV and next S, and the two never
+// compete for the MUFU unit.  Without the token they fall into lock-step and
+// the tensor pipe idles half the time.  3 of every 16 exponentials run on the
+// FMA pipe (exp2_poly) so one warpgroup's turn is shorter than the other
+// tile's MMA work.
 #pragma once
 
 #include "fe_ptx.cuh"
@@ -49,16 +61,27 @@ struct FwdCfg {
   static constexpr int OFF_K = 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
   static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
-  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
-  static constexpr int NBAR = 1 + 4 * STAGES + 7;
+  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain,
+  // turn[2]
+  static constexpr int NBAR = 1 + 4 * STAGES + 9;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment slack
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 384;
 };
+
+// Exponentials per 16 computed by exp2_poly instead of MUFU ex2.
+constexpr int FWD_POLY = 0;
+// Softmax warpgroups take turns for their exponentials (see header).
+constexpr bool FWD_TURNS = false;
+
+constexpr uint32_t FWD_REGS_HIGH = 216;
+constexpr uint32_t FWD_REGS_LOW = 64;
+// Registers per thread the launch must provide for the split above.
+constexpr int FWD_REGS_NEEDED = (2 * 128 * FWD_REGS_HIGH + 128 * FWD_REGS_LOW + 383) / 384;
 
 __device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     fe_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const FwdParams p) {
   using C = FwdCfg<DP>;
@@ -74,20 +97,35 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
+  uint64_t* turn = drain + 1;  // turn[t]: warpgroup t may start its exponentials
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
 
-  // ---- work item: (query block, b, hkv, g), heaviest query block first ----
+  // ---- work item: (query block, b, hkv, g) ----
+  // Causal: heaviest query blocks first (longest-processing-time order), the G
+  // heads of a group adjacent so they share K/V in L2.  Non-causal: every
+  // block costs the same, so the blocks of one head are adjacent instead and
+  // share that head's K/V.
   int item = blockIdx.x;
-  const int g = item % p.G;
-  item /= p.G;
-  const int hkv = item % p.Hkv;
-  item /= p.Hkv;
-  const int b = item % p.B;
-  const int rank = item / p.B;
+  int g, hkv, b, rank;
+  if (p.causal) {
+    g = item % p.G;
+    item /= p.G;
+    hkv = item % p.Hkv;
+    item /= p.Hkv;
+    b = item % p.B;
+    rank = item / p.B;
+  } else {
+    rank = item % p.num_blocks;
+    item /= p.num_blocks;
+    g = item % p.G;
+    item /= p.G;
+    hkv = item % p.Hkv;
+    b = item / p.Hkv;
+  }
   int blk;
   if (p.blocks != nullptr) {
     blk = p.blocks[rank];
@@ -117,6 +155,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&o_full[t], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(&turn[0], 4);
+    mbar_init(&turn[1], 4);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -130,6 +170,8 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_holder;
   const uint64_t TO = p.timeout_ns;
 
+  if (warp >= 8) {
+  setmaxnreg_dec<FWD_REGS_LOW>();
   if (warp == 8) {
     // ------------------------------------------------------------ producer --
     if (lane == 0 && nmax > 0) {
@@ -180,22 +222,30 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
+      // Descriptors are computed once; a k-step or a stage only moves the
+      // start-address field (address >> 4 in the low 14 bits), so it is a
+      // plain add on the 64-bit descriptor.
+      const uint64_t dq = smem_desc_sw128(q_addr, 16, 1024);
+      const uint64_t dk = smem_desc_sw128(k_addr, 16, 1024);
+      const uint64_t dv = smem_desc_sw128(v_addr, 16384, 1024);
+      constexpr uint64_t TILE16 = C::TILE >> 4;
       auto issue_s = [&](int t, int s) {
-        const uint32_t qa = q_addr + t * C::TILE;
-        const uint32_t ka = k_addr + s * C::TILE;
+        const uint64_t a = dq + t * TILE16;
+        const uint64_t bb = dk + s * TILE16;
+        const uint32_t d = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_ss(tmem + t * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024), ID_S,
-                  kk > 0);
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          umma_ss(d, a + off, bb + off, ID_S, kk > 0);
         }
       };
       auto issue_pv = [&](int t, int s, int j) {
-        const uint32_t va = v_addr + s * C::TILE;
+        const uint64_t bb = dv + s * TILE16;
+        const uint32_t d = tmem + 256 + t * DP;
+        const uint32_t pa = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(tmem + 256 + t * DP, tmem + t * 128 + kk * 8, smem_desc_sw128(va + kk * 2048, 16384, 1024), ID_PV,
-                  (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(d, pa + kk * 8, bb + static_cast<uint64_t>(kk * (2048 >> 4)), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, TO, abort_flag);
@@ -248,7 +298,9 @@ __global__ void __launch_bounds__(320, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, TO, abort_flag);
     }
+  }
   } else {
+    setmaxnreg_inc<FWD_REGS_HIGH>();
     // ------------------------------------------------------------- softmax --
     const int t = warp >> 2;
     const int nt = t == 0 ? n0 : n1;
@@ -259,6 +311,10 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + 256 + t * DP;
     const float sc = p.sc;
+    // Positive scale: max on raw logits, scale folded into one FFMA per
+    // element.  Otherwise scale first and use an effective scale of 1.
+    const bool sc_pos = sc > 0.f;
+    const float sce = sc_pos ? sc : 1.0f;
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
@@ -274,21 +330,22 @@ __global__ void __launch_bounds__(320, 1)
       }
       const int kbase = j * 128;
       const bool masked = (kbase + 128 > p.N) || (p.causal && kbase + 127 > rbase);
-      float mx = -INFINITY;
-      if (masked) {
-        const int lim = p.causal ? min(p.N - 1, row) : (p.N - 1);
+      if (!sc_pos) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          x[c] = (kbase + c <= lim) ? x[c] * sc : -INFINITY;
-          mx = fmaxf(mx, x[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          x[c] = x[c] * sc;
-          mx = fmaxf(mx, x[c]);
-        }
+        for (int c = 0; c < 128; ++c) x[c] *= sc;
       }
+      if (masked) {
+        const int lim = (p.causal ? min(p.N - 1, row) : (p.N - 1)) - kbase;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
+      }
+      // Row max: 3-input max, eight independent chains.
+      float mm[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mm[c] = x[c];
+#pragma unroll
+      for (int c = 8; c < 128; c += 2) mm[(c >> 1) & 7] = fmax3(mm[(c >> 1) & 7], x[c], x[c + 1]);
+      const float mx = fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7])) * sce;
       const float m_new = fmaxf(m_used, mx);
       if (j == 0) {
         m_used = m_new;
@@ -307,15 +364,51 @@ __global__ void __launch_bounds__(320, 1)
         }
         tmem_wait_st();
       }
-      float sum0 = 0.f, sum1 = 0.f;
+      // Wait for this warpgroup's turn (the other one has finished the
+      // exponentials of its previous tile).
+      {
+        bool wait_turn;
+        uint32_t par;
+        if (t == 0) {
+          wait_turn = (j >= 1) && (j - 1 < n1);
+          par = (j - 1) & 1;
+        } else {
+          wait_turn = j < n0;
+          par = j & 1;
+        }
+        if (FWD_TURNS && wait_turn) {
+          ok = warp_all(mbar_wait(&turn[t], par, TO, abort_flag));
+          if (!ok) break;
+        }
+      }
+      // p = 2^(x*sc - m): packed FP32x2 FMA for the arguments, MUFU ex2 for
+      // the exponentials (FWD_POLY of every 16 on the FMA pipe instead),
+      // packed adds into four pair accumulators for the row sum.
+      const uint64_t sc2 = f2_pack(sce, sce);
+      const uint64_t nm2 = f2_pack(-m_used, -m_used);
+      uint64_t acc2[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
       uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(x[2 * c] - m_used);
-        const float p1 = ex2_approx(x[2 * c + 1] - m_used);
-        sum0 += p0;
-        sum1 += p1;
-        pk[c] = pack2<BF16>(p0, p1);
+      for (int c = 0; c < 128; c += 2) {
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, nm2), a0, a1);
+        const float p0 = ((c & 15) >= 16 - FWD_POLY) ? exp2_poly(a0) : ex2_approx(a0);
+        const float p1 = (((c + 1) & 15) >= 16 - FWD_POLY) ? exp2_poly(a1) : ex2_approx(a1);
+        acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
+        pk[c >> 1] = pack2<BF16>(p0, p1);
+      }
+      float sacc[8];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) f2_unpack(acc2[c], sacc[2 * c], sacc[2 * c + 1]);
+      const float sum0 = (sacc[0] + sacc[1]) + (sacc[2] + sacc[3]);
+      const float sum1 = (sacc[4] + sacc[5]) + (sacc[6] + sacc[7]);
+      // Pass the turn to the other warpgroup if it has a tile to match.
+      {
+        const bool give = FWD_TURNS && ((t == 0) ? (j < n1) : (j + 1 < n0));
+        __syncwarp();
+        if (give && lane == 0) mbar_arrive(&turn[t ^ 1]);
       }
       l += sum0 + sum1;
       tmem_st32(tS, pk);

@@ -245,6 +245,54 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ---------------------------------------------- packed FP32 pairs (sm_100) --
+// Two FP32 lanes in one 64-bit register pair; fma/add.rn.f32x2 issue once for
+// both (same IEEE rounding per lane as the scalar instructions).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA pipe, for exponentials offloaded from the MUFU unit.
+// Range reduction x = n + f, n = rint(x), f in [-1/2, 1/2] (rounding by the
+// 1.5*2^23 shift), 2^f by a degree-4 polynomial whose coefficients minimise
+// the maximum relative error on [-1/2, 1/2] (Remez exchange; regenerate with
+// csrc/fit_exp2.py: max relative error 2.7e-6 in FP32 Horner form), and 2^n
+// added to the exponent field.  Inputs below -125 (including -inf) give 0.
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -125.0f);
+  const float t = xc + 12582912.0f;  // 1.5 * 2^23: rint(xc) lands in the low mantissa bits
+  const float n = t - 12582912.0f;
+  const float f = xc - n;
+  float p = 0.009570102207362652f;
+  p = fmaf(p, f, 0.05591785907745361f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  const float r = __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+  return x < -125.0f ? 0.0f : r;
+}
+
 // Pack two FP32 values into one 32-bit word of 16-bit elements, `lo` in the
 // low half (the element with the smaller K index).
 template <bool BF16>
@@ -256,6 +304,19 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   }
   return r;
+}
+
+// Per-warpgroup register budget changes (all four warps of a warpgroup
+// execute the same one).  The increases of a block must fit in the registers
+// released by its decreases plus the block's launch allocation; the host
+// checks the compiled register count before launching such a kernel.
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(R));
+}
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(R));
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

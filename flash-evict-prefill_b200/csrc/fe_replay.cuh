@@ -14,7 +14,9 @@
 // The per-query normaliser and weight fold into one exponent bias:
 //   w_q / l_q * exp2(x - m_q) = exp2(x - bias_q),
 //   bias_q = m_q + log2(l_q) - decay*log2(e)*(q - (N-1))
-// with bias_q = +inf for rows outside the window or past N.  Query tiles whose
+// with bias_q = +inf for rows outside the window or past N.  The reduction is
+// MUFU-bound, so 4 of every 16 exponentials run on the FMA pipe (exp2_poly,
+// relative error < 3e-6) and the exponent arithmetic uses packed FP32x2.  Query tiles whose
 // every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
 //
 // Roles (192 threads): warps 0-3 reduce (thread = key), warp 4 TMA producer,
@@ -39,6 +41,10 @@ struct ReplayParams {
   int causal, weighted;
   uint64_t timeout_ns;
 };
+
+// Exponentials per 16 evaluated by exp2_poly (FMA pipe) instead of MUFU ex2;
+// the replay is MUFU-bound (16384 exponentials per 512-cycle S^T MMA).
+constexpr int REPLAY_POLY = 4;
 
 template <int DP>
 struct ReplayCfg {
@@ -106,13 +112,14 @@ __global__ void __launch_bounds__(192, 2)
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
 
-  // ---- work item: (key tile, b, hkv); key tile 0 (most causal work) first ----
-  int item = blockIdx.x;
-  const int hkv = item % p.Hkv;
-  item /= p.Hkv;
-  const int b = item % p.B;
-  const int kt = item / p.B;
+  // ---- work item: (key tile, b, hkv), key tiles of one (b, hkv) adjacent so
+  // the CTAs that stream the same Q rows run together and share them in L2 ----
   const int nqt = (p.N + 127) / 128;
+  int item = blockIdx.x;
+  const int kt = item % nqt;
+  item /= nqt;
+  const int hkv = item % p.Hkv;
+  const int b = item / p.Hkv;
   const int qt_lo = max(p.s_lo / 128, p.causal ? kt : 0);
   const uint32_t* map = nullptr;
 
@@ -224,28 +231,42 @@ __global__ void __launch_bounds__(192, 2)
     double acc = 0.0;
     ReplayItems it;
     it.init(qt_lo, nqt, p.G, map);
+    // Row statistics {m, l} of an item's 128 query rows (4 per lane).
+    auto load_stats = [&](const ReplayItems& x, float2* dst) {
+      const float2* st =
+          reinterpret_cast<const float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hkv * p.G + x.g) * p.N;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = x.qt * 128 + static_cast<int>(lane) + 32 * u;
+        dst[u] = (q < p.N && q >= p.s_lo) ? st[q] : make_float2(0.f, 1.f);
+      }
+    };
+    float2 ml_next[4];
+    if (it.valid()) load_stats(it, ml_next);
     uint32_t i = 0;
     bool ok = true;
     for (; it.valid(); it.next(), ++i) {
       const int sb = i & 1;
       // Exponent bias of the item's 128 query columns; each warp keeps its own
       // copy (lane l fills columns l, l+32, l+64, l+96) so the warpgroup needs
-      // no cross-warp barrier.
-      __syncwarp();
+      // no cross-warp barrier.  The row statistics of the next item are loaded
+      // here too, so their latency overlaps this item's reduction.
+      const float2 ml_cur[4] = {ml_next[0], ml_next[1], ml_next[2], ml_next[3]};
+      const int qcur = it.qt * 128;
       {
-        const int hq = hkv * p.G + it.g;
-        const float2* st = reinterpret_cast<const float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hq) * p.N;
+        ReplayItems nx = it;
+        nx.next();
+        if (nx.valid()) load_stats(nx, ml_next);
+      }
+      __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int c = static_cast<int>(lane) + 32 * u;
-          const int q = it.qt * 128 + c;
-          float bias = INFINITY;
-          if (q < p.N && q >= p.s_lo) {
-            const float2 ml = st[q];
-            bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml.x + log2f(ml.y));
-          }
-          wbias[c] = bias;
-        }
+      for (int u = 0; u < 4; ++u) {
+        const int c = static_cast<int>(lane) + 32 * u;
+        const int q = qcur + c;
+        float bias = INFINITY;
+        if (q < p.N && q >= p.s_lo)
+          bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml_cur[u].x + log2f(ml_cur[u].y));
+        wbias[c] = -bias;  // stored negated: the exponent is x*sc + wbias
       }
       __syncwarp();
       ok = warp_all(mbar_wait(&s_full[sb], (i >> 1) & 1, TO, abort_flag));
@@ -260,31 +281,40 @@ __global__ void __launch_bounds__(192, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
-      const float4* bias4 = reinterpret_cast<const float4*>(wbias);
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      if (p.causal && it.qt == kt) {
-        // Diagonal tile: query column c contributes only when c >= kr.
+      // exp2(x*sc - bias_q) summed over the 128 query columns: packed FP32x2
+      // FMA for the exponents, REPLAY_POLY of every 16 exponentials on the FMA
+      // pipe (exp2_poly) and the rest on MUFU, packed adds into four pair
+      // accumulators.  Diagonal tile: columns q < key are masked to -inf.
+      const float4* nb4 = reinterpret_cast<const float4*>(wbias);
+      const uint64_t sc2 = f2_pack(sc, sc);
+      const bool diag = p.causal && it.qt == kt;
+      uint64_t acc2[4];
 #pragma unroll
-        for (int c4 = 0; c4 < 32; ++c4) {
-          const float4 bb = bias4[c4];
-          const int c = c4 * 4;
-          a0 += (c + 0 >= kr) ? ex2_approx(fmaf(x[c + 0], sc, -bb.x)) : 0.f;
-          a1 += (c + 1 >= kr) ? ex2_approx(fmaf(x[c + 1], sc, -bb.y)) : 0.f;
-          a2 += (c + 2 >= kr) ? ex2_approx(fmaf(x[c + 2], sc, -bb.z)) : 0.f;
-          a3 += (c + 3 >= kr) ? ex2_approx(fmaf(x[c + 3], sc, -bb.w)) : 0.f;
-        }
-      } else {
+      for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
 #pragma unroll
-        for (int c4 = 0; c4 < 32; ++c4) {
-          const float4 bb = bias4[c4];
-          const int c = c4 * 4;
-          a0 += ex2_approx(fmaf(x[c + 0], sc, -bb.x));
-          a1 += ex2_approx(fmaf(x[c + 1], sc, -bb.y));
-          a2 += ex2_approx(fmaf(x[c + 2], sc, -bb.z));
-          a3 += ex2_approx(fmaf(x[c + 3], sc, -bb.w));
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 nb = nb4[c4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = c4 * 4 + h * 2;
+          float a0, a1;
+          f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, h == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w)), a0,
+                    a1);
+          if (diag) {
+            a0 = (c >= kr) ? a0 : -INFINITY;
+            a1 = (c + 1 >= kr) ? a1 : -INFINITY;
+          }
+          const float p0 = ((c & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
+          const float p1 = (((c + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
+          acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
         }
       }
-      acc += static_cast<double>((a0 + a1) + (a2 + a3));
+      float a0, a1, a2, a3, a4, a5, a6, a7;
+      f2_unpack(acc2[0], a0, a1);
+      f2_unpack(acc2[1], a2, a3);
+      f2_unpack(acc2[2], a4, a5);
+      f2_unpack(acc2[3], a6, a7);
+      acc += static_cast<double>(((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7)));
     }
     if (ok && key < p.N) {
       float vn = 1.0f;

@@ -48,6 +48,7 @@ SIGNATURES = {
     "fe_device_status": (_INT, [_INT, _INT, ctypes.POINTER(_INT)]),
     "fe_set_watchdog_ns": (None, [_I64]),
     "fe_watchdog_selftest": (_INT, [_I64, _VP]),
+    "fe_selftest_exp2": (_INT, [_VP, _VP, _VP, _I64, _VP]),
     "fe_last_error": (ctypes.c_char_p, []),
     "fe_abi_version": (_INT, []),
 }

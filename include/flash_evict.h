@@ -142,6 +142,12 @@ FE_API void fe_set_watchdog_ns(int64_t ns);
  * exercise the timeout path without hanging a GPU. */
 FE_API int fe_watchdog_selftest(int64_t timeout_ns, void* stream);
 
+/* Evaluate the kernels' two exp2 implementations elementwise: out_poly = the
+ * FMA-pipe polynomial (Cody-Waite reduction + degree-4 minimax, used for a
+ * share of the softmax exponentials), out_mufu = the hardware ex2.approx.
+ * Diagnostic for tests; no counterpart in the reference (Triton's exp2). */
+FE_API int fe_selftest_exp2(const float* in, float* out_poly, float* out_mufu, int64_t n, void* stream);
+
 /* Message describing the last error returned on the calling thread. */
 FE_API const char* fe_last_error(void);
 

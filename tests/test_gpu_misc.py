@@ -170,3 +170,25 @@ def test_config5_batched_mha_noncausal_h2o_sampled():
         np.testing.assert_allclose(out[bi, hi, rows].float().cpu().numpy(), ro[0, 0, rows], atol=0.004, rtol=0.006)
         np.testing.assert_allclose(imp[bi, hi].cpu().numpy(), ri[0, 0], atol=1e-3, rtol=1e-3)
     assert (~mask).sum(-1).eq(410).all()
+
+
+def test_exp2_polynomial_error_bound():
+    """The FMA-pipe exp2 used for part of the softmax: relative error within
+    the fitted bound (2.7e-6) of float64 exp2 over the softmax's input range,
+    exact zero below -125 and for -inf; the MUFU path within 2^-21."""
+    xs = torch.cat([torch.linspace(-125.0, 8.0, 2_000_001), torch.tensor([-125.5, -126.0, -200.0, -1e30,
+                                                                            float("-inf")])]).cuda()
+    poly = torch.empty_like(xs)
+    mufu = torch.empty_like(xs)
+    _lib.check(_lib.load().fe_selftest_exp2(xs.data_ptr(), poly.data_ptr(), mufu.data_ptr(), xs.numel(),
+                                            torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    x64 = xs.double()
+    ref = torch.exp2(x64)
+    main = xs >= -125.0
+    rel_poly = ((poly.double() - ref).abs() / ref)[main]
+    assert rel_poly.max().item() < 3e-6, rel_poly.max().item()
+    assert torch.all(poly[~main] == 0)
+    normal = xs >= -126.0
+    rel_mufu = ((mufu.double() - ref).abs() / ref)[normal]
+    assert rel_mufu.max().item() < 2 ** -21
