@@ -45,15 +45,19 @@ WORKLOADS = {
     "c2": dict(b=1, hq=32, hkv=8, n=8192, d=128, dtype=torch.bfloat16, causal=True, budget=1024,
                kw=dict(recency_decay=0.1, reserved_recent=64), sinks=False, qscale=128 ** -0.25,
                desc="Llama-3-8B-shaped B1 Hq32 Hkv8 N8192 D128 bf16 causal, decay 0.1, reserved 64, budget 1024"),
+    "c4": dict(b=1, hq=32, hkv=8, n=131072, d=128, dtype=torch.bfloat16, causal=True, budget=1024,
+               kw=dict(recency_decay=0.1, reserved_recent=64), sinks=False, qscale=1.0,
+               desc="Long context B1 Hq32 Hkv8 N131072 D128 bf16 causal, decay 0.1, reserved 64, budget 1024; "
+                    "query blocks sharded across GPUs, one NCCL all-reduce of the FP32 scores"),
     "c5": dict(b=8, hq=32, hkv=32, n=4096, d=128, dtype=torch.float16, causal=False, budget=410,
                kw=dict(value_weighted=False), sinks=False, qscale=30.0, transposed=True, zero_v=0.05,
                desc="Batched MHA B8 Hq=Hkv=32 N4096 D128 fp16 noncausal, [B,N,H,D] strides, q x30, 5% zero V "
                     "rows, H2O, budget 410"),
 }
 
-# DRAM traffic of one attention-forward launch at c3, from the ncu capture
-# summarised in profiles/ (None until captured).
-TRAFFIC_PER_FWD_LAUNCH = None
+# DRAM bytes (read + write) of one attention-forward launch per workload, from
+# the ncu capture summarised in profiles/ (absent until captured).
+TRAFFIC_PER_FWD_LAUNCH = {}
 
 
 def peaks():
@@ -197,7 +201,8 @@ def run_reference(args, w):
 
 def run_ours(args, w):
     import torch.distributed as dist
-    from flash_evict import _lib, evict, prefill
+    from flash_evict import _lib, evict
+    from flash_evict.distributed import evict_query_sharded, head_unit_plan
     from flash_evict.prefill import _evict_impl
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -208,7 +213,12 @@ def run_ours(args, w):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    q, k, v = make_inputs(w, 1000 + rank, dev)
+    # replica: every rank its own batch element (weak scaling, no collective)
+    # query:   one problem, query blocks sharded, one score all-reduce (strong)
+    # heads:   one problem, (batch, kv-head) units sharded, no collective (strong)
+    mode = "query" if args.workload == "c4" else ("heads" if (args.workload == "c5" and world > 1) else "replica")
+    seed = 1000 + (rank if mode == "replica" else 0)
+    q, k, v = make_inputs(w, seed, dev)
     kw = dict(w["kw"])
     budget = w["budget"]
     recent = kw.pop("reserved_recent", 0)
@@ -216,6 +226,20 @@ def run_ours(args, w):
     kw["causal"] = w["causal"]
     f_attn, f_rep, f_rep_all = flops(w)
     stream = torch.cuda.current_stream(dev)
+    g = w["hq"] // w["hkv"]
+    runs = head_unit_plan(w["b"], w["hkv"], world)[rank] if mode == "heads" else None
+
+    def step(qq, kk, vv, marks=None):
+        if mode == "replica":
+            return _evict_impl(qq, kk, vv, budget, 0, recent, pool, marks, kw)
+        if mode == "query":
+            return evict_query_sharded(qq, kk, vv, budget, reserved_recent=recent, pool_kernel=pool, _marks=marks,
+                                       **kw)
+        res = []
+        for b, h0, h1 in runs:
+            res.append(_evict_impl(qq[b:b + 1, h0 * g:h1 * g], kk[b:b + 1, h0:h1], vv[b:b + 1, h0:h1], budget, 0,
+                                   recent, pool, marks, kw))
+        return res
 
     def barrier():
         if world > 1:
@@ -229,26 +253,29 @@ def run_ours(args, w):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    for _ in range(args.warmup):
+        step(q, k, v)
+    if args.profile:
+        # Short run for ncu: warm-up plus K steps, nothing else.
+        for _ in range(args.steps):
+            step(q, k, v)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            print(json.dumps({"profile_run": args.workload, "mode": mode, "steps": args.steps,
+                              "warmup": args.warmup, "device_status": _lib.device_status(local)}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     # ---------------- device-resident timed region: value + roofline -------
-    n_ev = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_ev)]
-    slot = {"i": -1}
-    stages = {"start": 0, "attention": 1, "replay": 2, "select": 3}
+    events = [[] for _ in range(args.steps)]
+    cur = {"i": -1}
 
     def marks(stage):
-        if slot["i"] >= 0:
-            ev[slot["i"]][stages[stage]].record(stream)
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)
+        events[cur["i"]].append((stage, e))
 
-    for _ in range(args.warmup):
-        _evict_impl(q, k, v, budget, 0, recent, pool, None, kw)
-    if args.profile:
-        # Short run for ncu: warm-up plus K evict() steps, nothing else.
-        for _ in range(args.steps):
-            _evict_impl(q, k, v, budget, 0, recent, pool, None, kw)
-        torch.cuda.synchronize(dev)
-        print(json.dumps({"profile_run": args.workload, "steps": args.steps, "warmup": args.warmup,
-                          "launches_per_step": 3, "device_status": _lib.device_status(local)}), flush=True)
-        return
     clocks = Clocks(local)
     barrier()
     clocks.start()
@@ -256,45 +283,33 @@ def run_ours(args, w):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for i in range(args.steps):
-        slot["i"] = i
-        _evict_impl(q, k, v, budget, 0, recent, pool, marks, kw)
+        cur["i"] = i
+        step(q, k, v, marks)
     t1.record(stream)
     barrier()
     clk = clocks.stop()
-    slot["i"] = -1
     total_ms = max_over_ranks(t0.elapsed_time(t1))
-    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    rep_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    sel_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    stage_ms = {}
+    for evs in events:
+        for (a, ea), (b_, eb) in zip(evs, evs[1:]):
+            if b_ != "start":
+                stage_ms[b_] = stage_ms.get(b_, 0.0) + ea.elapsed_time(eb)
+    stage_ms = {kk_: vv_ / args.steps for kk_, vv_ in stage_ms.items()}
     ms_per_step = total_ms / args.steps
-    step_flops = f_attn + f_rep
-    value = step_flops * world / (ms_per_step * 1e-3) / 1e12
-
-    # ---------------- attention-only (same forward kernel, no replay) -------
-    prefill_kw = dict(w["kw"])
-    prefill_kw.pop("reserved_recent", None)
-    prefill_kw.pop("pool_kernel", None)
-    for _ in range(2):
-        prefill(q, k, v, causal=w["causal"], score=False)
-    barrier()
-    a0 = torch.cuda.Event(enable_timing=True)
-    a1 = torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    for _ in range(args.steps):
-        prefill(q, k, v, causal=w["causal"], score=False)
-    a1.record(stream)
-    barrier()
-    attn_only_ms = max_over_ranks(a0.elapsed_time(a1)) / args.steps
+    total_flops = (f_attn + f_rep) * (world if mode == "replica" else 1)
+    value = total_flops / (ms_per_step * 1e-3) / 1e12
+    attn_ms = stage_ms.get("attention", float("nan"))
+    # FLOPs of this rank's attention launches (its share of the problem)
+    my_attn_flops = f_attn if mode == "replica" else f_attn / world
+    attn_ms_max = max_over_ranks(attn_ms)
 
     # ---------------- end to end: host buffers, copies inside the region ---
     hq_, hk_, hv_ = (t.detach().cpu().pin_memory() for t in (q, k, v))
     dq, dk, dv = (torch.empty(t.shape, dtype=t.dtype, device=dev) for t in (hq_, hk_, hv_))
-    if w.get("transposed"):
-        dq, dk, dv = (t for t in (dq, dk, dv))
     h2d = sum(t.numel() * t.element_size() for t in (hq_, hk_, hv_))
-    outs = None
     host_out = None
     e2e_steps = max(2, min(args.steps, 10))
+    barrier()
     for it in range(e2e_steps + 1):
         if it == 1:
             barrier()
@@ -304,16 +319,19 @@ def run_ours(args, w):
         dq.copy_(hq_, non_blocking=True)
         dk.copy_(hk_, non_blocking=True)
         dv.copy_(hv_, non_blocking=True)
-        outs = evict(dq, dk, dv, budget, reserved_recent=recent, pool_kernel=pool, **kw)
+        res = step(dq, dk, dv)
+        flat = []
+        for r_ in (res if isinstance(res, list) else [res]):
+            flat.extend(t for t in r_ if torch.is_tensor(t))
         if host_out is None:
-            host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
-        for h_, d_ in zip(host_out, outs):
+            host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in flat]
+        for h_, d_ in zip(host_out, flat):
             h_.copy_(d_, non_blocking=True)
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
     d2h = sum(t.numel() * t.element_size() for t in host_out)
-    e2e_value = step_flops * world / (e2e_ms * 1e-3) / 1e12
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
 
     status = _lib.device_status(local)
     if world > 1:
@@ -324,30 +342,40 @@ def run_ours(args, w):
         return
 
     burst, sustained, hbm, src = peaks()
-    achieved = f_attn / (fwd_ms * 1e-3) / 1e12
+    achieved = my_attn_flops / (attn_ms * 1e-3) / 1e12
+    launches_per_step = 3 * (len(runs) if mode == "heads" else 1)
+    parallelism = {"replica": f"replicas x{world} (one batch element per GPU, no collective)" if world > 1
+                   else "single GPU",
+                   "query": f"query-block sharded x{world}, one NCCL all_reduce(SUM) of [B,Hkv,N] FP32 scores",
+                   "heads": f"(batch, kv-head) units sharded x{world}, no collective"}[mode]
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if mode == "replica" else "strong",
         "vs_baseline": None, "dtype": "f16" if w["dtype"] == torch.float16 else "bf16", "data": "synthetic",
-        "config": {"workload": args.workload + ": " + w["desc"], "global_batch": w["b"] * world,
-                   "seq_len": w["n"], "parallelism": f"replicas x{world} (batch element per GPU, no collective)"
-                   if world > 1 else "single GPU", "l2": "inputs larger than L2 (no flush)",
-                   "flops_per_step": step_flops, "attention_flops": f_attn, "replay_flops": f_rep,
+        "config": {"workload": args.workload + ": " + w["desc"], "global_batch": w["b"] * (world if mode == "replica"
+                                                                                            else 1),
+                   "seq_len": w["n"], "parallelism": parallelism, "l2": "inputs larger than L2 (no flush)",
+                   "flops_per_step": total_flops, "attention_flops": f_attn, "replay_flops": f_rep,
                    "replay_flops_without_underflow_skip": f_rep_all},
-        "overhead_vs_attention_only": ms_per_step / attn_only_ms,
-        "attention_only_ms": attn_only_ms,
-        "kernel_ms": {"attention": fwd_ms, "replay": rep_ms, "select": sel_ms},
-        "pct_of_peak": {"value_vs_sustained": value / world / sustained, "value_vs_burst": value / world / burst},
+        "overhead_vs_attention_only": ms_per_step / attn_ms_max if mode != "query" else None,
+        "attention_only_ms": attn_ms_max,
+        "kernel_ms": stage_ms,
+        "pct_of_peak": {"per_gpu_value_vs_sustained": value / world / sustained,
+                        "per_gpu_value_vs_burst": value / world / burst},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
-                     "frac": achieved / sustained, "traffic": TRAFFIC_PER_FWD_LAUNCH,
-                     "kernel": "fe_fwd_kernel (attention forward)",
+                     "frac": achieved / sustained, "traffic": TRAFFIC_PER_FWD_LAUNCH.get(args.workload)
+                     if mode == "replica" and world == 1 else None,
+                     "kernel": "fe_fwd_kernel (attention forward), rank 0",
                      "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a multi-second loop)"},
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }
+    if mode == "query":
+        line["overhead_vs_attention_only"] = ms_per_step / attn_ms_max
     if world == 1 and not args.no_cpu_baseline:
         val, desc, threads = cpu_oracle_sample(w, q, k, v, seconds=10.0)
         line["cpu_baseline"] = {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}

@@ -80,6 +80,49 @@ constexpr int FWD_REGS_NEEDED = (2 * 128 * FWD_REGS_HIGH + 128 * FWD_REGS_LOW + 
 
 __device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
 
+// One softmax exponential pass over a 128-column row: p = 2^(x*sce - m) with
+// packed FP32x2 FMAs for the arguments, MUFU ex2 for the exponentials (POLY of
+// every 16 on the FMA pipe instead), packed adds into four pair accumulators,
+// and optionally the largest argument.  Returns the row sum; P is packed into pk.
+template <bool BF16, int POLY, bool TRACK_MAX>
+__device__ __forceinline__ float softmax_exp_pass(const float (&x)[128], float sce, float m, uint32_t (&pk)[64],
+                                                  float& amax) {
+  const uint64_t sc2 = f2_pack(sce, sce);
+  const uint64_t nm2 = f2_pack(-m, -m);
+  uint64_t acc2[4];
+  float am[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    acc2[c] = 0ull;
+    am[c] = -INFINITY;
+  }
+#pragma unroll
+  for (int c = 0; c < 128; c += 2) {
+    float a0, a1;
+    f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, nm2), a0, a1);
+    if (TRACK_MAX) am[(c >> 1) & 3] = fmax3(am[(c >> 1) & 3], a0, a1);
+    const float p0 = ((c & 15) >= 16 - POLY) ? exp2_poly(a0) : ex2_approx(a0);
+    const float p1 = (((c + 1) & 15) >= 16 - POLY) ? exp2_poly(a1) : ex2_approx(a1);
+    acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
+    pk[c >> 1] = pack2<BF16>(p0, p1);
+  }
+  amax = fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3]));
+  float sacc[8];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) f2_unpack(acc2[c], sacc[2 * c], sacc[2 * c + 1]);
+  return ((sacc[0] + sacc[1]) + (sacc[2] + sacc[3])) + ((sacc[4] + sacc[5]) + (sacc[6] + sacc[7]));
+}
+
+// Row maximum of the scaled logits (x * sce), eight independent 3-input-max chains.
+__device__ __forceinline__ float row_max_scaled(const float (&x)[128], float sce) {
+  float mm[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) mm[c] = x[c];
+#pragma unroll
+  for (int c = 8; c < 128; c += 2) mm[(c >> 1) & 7] = fmax3(mm[(c >> 1) & 7], x[c], x[c + 1]);
+  return fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7])) * sce;
+}
+
 template <bool BF16, int DP>
 __global__ void __launch_bounds__(384, 1)
     fe_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -339,14 +382,11 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
         for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
       }
-      // Row max: 3-input max, eight independent chains.
-      float mm[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) mm[c] = x[c];
-#pragma unroll
-      for (int c = 8; c < 128; c += 2) mm[(c >> 1) & 7] = fmax3(mm[(c >> 1) & 7], x[c], x[c + 1]);
-      const float mx = fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7])) * sce;
-      const float m_new = fmaxf(m_used, mx);
+      // Row max first.  The max used for the exponentials only moves when the
+      // true max exceeds it by more than 2^8 (lazy rescale); tracking the max
+      // inside the exponential pass instead was measured slower (extreme
+      // logits force frequent redo passes).
+      const float m_new = fmaxf(m_used, row_max_scaled(x, sce));
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
@@ -381,36 +421,16 @@ __global__ void __launch_bounds__(384, 1)
           if (!ok) break;
         }
       }
-      // p = 2^(x*sc - m): packed FP32x2 FMA for the arguments, MUFU ex2 for
-      // the exponentials (FWD_POLY of every 16 on the FMA pipe instead),
-      // packed adds into four pair accumulators for the row sum.
-      const uint64_t sc2 = f2_pack(sce, sce);
-      const uint64_t nm2 = f2_pack(-m_used, -m_used);
-      uint64_t acc2[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
       uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 128; c += 2) {
-        float a0, a1;
-        f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, nm2), a0, a1);
-        const float p0 = ((c & 15) >= 16 - FWD_POLY) ? exp2_poly(a0) : ex2_approx(a0);
-        const float p1 = (((c + 1) & 15) >= 16 - FWD_POLY) ? exp2_poly(a1) : ex2_approx(a1);
-        acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
-        pk[c >> 1] = pack2<BF16>(p0, p1);
-      }
-      float sacc[8];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) f2_unpack(acc2[c], sacc[2 * c], sacc[2 * c + 1]);
-      const float sum0 = (sacc[0] + sacc[1]) + (sacc[2] + sacc[3]);
-      const float sum1 = (sacc[4] + sacc[5]) + (sacc[6] + sacc[7]);
+      float amax;
+      const float tile_sum = softmax_exp_pass<BF16, FWD_POLY, false>(x, sce, m_used, pk, amax);
       // Pass the turn to the other warpgroup if it has a tile to match.
       {
         const bool give = FWD_TURNS && ((t == 0) ? (j < n1) : (j + 1 < n0));
         __syncwarp();
         if (give && lane == 0) mbar_arrive(&turn[t ^ 1]);
       }
-      l += sum0 + sum1;
+      l += tile_sum;
       tmem_st32(tS, pk);
       tmem_st32(tS + 32, pk + 32);
       tmem_wait_st();

@@ -103,7 +103,7 @@ def evict_head_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recent
     return results
 
 
-def _cuda_partial(q, k, v, blocks, causal, scale, recency_decay, observation_window, value_weighted):
+def _cuda_partial(q, k, v, blocks, causal, scale, recency_decay, observation_window, value_weighted, marks=None):
     """This rank's attention rows and partial importance, on its GPU."""
     b, h, n, d = q.shape
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
@@ -112,10 +112,16 @@ def _cuda_partial(q, k, v, blocks, causal, scale, recency_decay, observation_win
     blk = torch.tensor(blocks, dtype=torch.int32, device=q.device)
     qv, kv, vv = _tma_view(q), _tma_view(k), _tma_view(v)
     with torch.cuda.device(q.device):
+        if marks:
+            marks("start")
         if len(blocks):
             _attention(qv, kv, vv, out, row_stats, causal, scale, query_blocks=blk)
+        if marks:
+            marks("attention")
         _replay(qv, kv, vv, row_stats, importance, causal, scale, recency_decay, observation_window,
                 value_weighted, query_blocks=blk)
+        if marks:
+            marks("replay")
     return out, importance
 
 
@@ -140,14 +146,22 @@ def _gather_rows(out, plan, rank, group):
 
 
 def _query_sharded(q, k, v, budget, recent, pool_kernel, causal, scale, recency_decay, observation_window,
-                   value_weighted, gather_output, group, partial_fn, select_fn):
+                   value_weighted, gather_output, group, partial_fn, select_fn, marks=None):
     rank, world = _world(group)
     plan = query_block_plan(q.shape[2], world, causal)
-    out, importance = partial_fn(q, k, v, plan[rank], causal, scale, recency_decay, observation_window,
-                                 value_weighted)
+    if marks:
+        out, importance = partial_fn(q, k, v, plan[rank], causal, scale, recency_decay, observation_window,
+                                     value_weighted, marks=marks)
+    else:
+        out, importance = partial_fn(q, k, v, plan[rank], causal, scale, recency_decay, observation_window,
+                                     value_weighted)
     if world > 1:
         dist.all_reduce(importance, op=dist.ReduceOp.SUM, group=group)
+    if marks:
+        marks("allreduce")
     indices, mask = select_fn(importance, budget, recent, pool_kernel)
+    if marks:
+        marks("select")
     if gather_output and world > 1:
         out = _gather_rows(out, plan, rank, group)
     return out, importance, indices, mask, plan[rank]
@@ -155,7 +169,7 @@ def _query_sharded(q, k, v, budget, recent, pool_kernel, causal, scale, recency_
 
 def evict_query_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recent=None, pool_kernel=1,
                         gather_output=False, causal=True, value_weighted=True, scale=None, block_q=32,
-                        block_k=64, recency_decay=0., observation_window=0):
+                        block_k=64, recency_decay=0., observation_window=0, _marks=None):
     """Query-block-sharded evict() for long contexts.
 
     Every rank passes the same full q/k/v (on its own GPU).  Returns
@@ -172,4 +186,4 @@ def evict_query_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recen
         return _select(importance, budget_, recent_, pool_, evict_mask=True)
 
     return _query_sharded(q, k, v, budget, recent, pool_kernel, causal, scale, recency_decay, observation_window,
-                          value_weighted, gather_output, group, _cuda_partial, select_fn)
+                          value_weighted, gather_output, group, _cuda_partial, select_fn, marks=_marks)
