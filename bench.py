@@ -55,9 +55,9 @@ WORKLOADS = {
                     "rows, H2O, budget 410"),
 }
 
-# DRAM bytes (read + write) of one attention-forward launch per workload, from
-# the ncu capture summarised in profiles/ (absent until captured).
-TRAFFIC_PER_FWD_LAUNCH = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# attention-forward launch, from the ncu capture in profiles/fe_fwd_kernel_c3.md.
+TRAFFIC_PER_FWD_LAUNCH = {"c3": 651232256 + 222683904}
 
 
 def peaks():

@@ -349,8 +349,11 @@ int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int6
   if (rc) return rc;
   const int64_t P = tokens - recent;
   const int64_t max_slice = 49152;  // keys per CTA held in shared memory (192 KiB)
+  // Cluster size: enough CTAs for the slice to fit in shared memory, and up
+  // to 8 for long rows (>= 4096 keys per CTA) so few rows still use many SMs.
   int cl = 1;
   while (cl < 16 && (P + cl - 1) / cl > max_slice) cl *= 2;
+  while (cl < 8 && P / (2 * cl) >= 4096) cl *= 2;
   if ((P + cl - 1) / cl > max_slice)
     return fail(FE_STATUS_UNSUPPORTED, "sequence length %lld exceeds the selection limit (%lld)", (long long)tokens,
                 (long long)(max_slice * 16));

@@ -12,8 +12,10 @@
 // it: larger value first, among equal values the lower index; NaN is the
 // largest value and -0.0 equals +0.0.
 //
-// One thread-block cluster of C CTAs per row; CTA r holds a contiguous slice
-// of the past region as order-preserving uint32 keys in shared memory.  The
+// One thread-block cluster of C CTAs per row (C grows with the row length so
+// that short batches still spread over several SMs); CTA r holds a
+// contiguous slice of the past region as order-preserving uint32 keys in
+// shared memory.  The
 // (budget-recent)-th largest key is found MSB-first with four 8-bit radix
 // passes whose histograms are merged through distributed shared memory.
 // Compaction walks each slice in index order (ballot/popc scans), so indices
@@ -148,9 +150,17 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const SelectP
       for (int i = threadIdx.x; i < 256; i += SEL_THREADS) hist[buf][i] = 0;
       __syncthreads();
     }
-    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
-      const uint32_t k = keys[i];
-      if ((k & pmask) == prefix) atomicAdd(&hist[buf][(k >> shift) & 255u], 1u);
+    // Warp-aggregated counting: the lanes holding the same digit elect one
+    // of them to add the group's count (scores are often concentrated in a
+    // few digits, which would otherwise serialise the shared-memory atomics).
+    for (int base = 0; base < len; base += SEL_THREADS) {
+      const int i = base + threadIdx.x;
+      const uint32_t k = i < len ? keys[i] : 0u;
+      const bool match = (i < len) && ((k & pmask) == prefix);
+      const uint32_t digit = match ? ((k >> shift) & 255u) : 0x100u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+      if (match && (threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
+        atomicAdd(&hist[buf][digit], static_cast<uint32_t>(__popc(peers)));
     }
     cluster.sync();
     if (threadIdx.x < 256) {
