@@ -23,6 +23,18 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+@pytest.fixture(scope="session", autouse=True)
+def _short_watchdog():
+    """Device-side waits in these tests last microseconds; a 0.5 s watchdog
+    makes a kernel that waits on something that never happens report a
+    timeout quickly instead of after the 2 s default per wait."""
+    import torch
+    if torch.cuda.is_available():
+        from flash_evict import _lib
+        _lib.load().fe_set_watchdog_ns(500_000_000)
+    yield
+
+
 @pytest.fixture(autouse=True)
 def _device_status(request):
     """After every GPU test: no kernel may have raised the device status word
