@@ -49,6 +49,12 @@ WORKLOADS = {
                kw=dict(recency_decay=0.1, reserved_recent=64), sinks=False, qscale=1.0,
                desc="Long context B1 Hq32 Hkv8 N131072 D128 bf16 causal, decay 0.1, reserved 64, budget 1024; "
                     "query blocks sharded across GPUs, one NCCL all-reduce of the FP32 scores"),
+    # The reference's own published A10G measurement (results/REPORT.md:90,
+    # fused_replay_topk at 32K: 333.041 ms): all-query scoring, 10 % budget.
+    "a10g32k": dict(b=1, hq=28, hkv=4, n=32768, d=128, dtype=torch.bfloat16, causal=True, budget=3277,
+                    kw=dict(), sinks=False, qscale=1.0,
+                    desc="reference benchmark shape B1 Hq28 Hkv4 N32768 D128 bf16 causal, all-query scoring, "
+                         "budget 10%"),
     "c5": dict(b=8, hq=32, hkv=32, n=4096, d=128, dtype=torch.float16, causal=False, budget=410,
                kw=dict(value_weighted=False), sinks=False, qscale=30.0, transposed=True, zero_v=0.05,
                desc="Batched MHA B8 Hq=Hkv=32 N4096 D128 fp16 noncausal, [B,N,H,D] strides, q x30, 5% zero V "

@@ -319,6 +319,21 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(R));
 }
 
+// Global load kept at its place in program order (volatile asm), used to
+// prefetch a value that is consumed much later: an ordinary load may be sunk
+// by the compiler to just before its first use.
+__device__ __forceinline__ float2 ld_global_f2_pinned(const float2* ptr) {
+  float2 r;
+  asm volatile("ld.global.nc.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(ptr));
+  return r;
+}
+
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -15,7 +15,7 @@
 //   w_q / l_q * exp2(x - m_q) = exp2(x - bias_q),
 //   bias_q = m_q + log2(l_q) - decay*log2(e)*(q - (N-1))
 // with bias_q = +inf for rows outside the window or past N.  The reduction is
-// MUFU-bound, so 4 of every 16 exponentials run on the FMA pipe (exp2_poly,
+// MUFU-bound, so 2 of every 16 exponentials run on the FMA pipe (exp2_poly,
 // relative error < 3e-6) and the exponent arithmetic uses packed FP32x2.  Query tiles whose
 // every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
 //
@@ -44,7 +44,7 @@ struct ReplayParams {
 
 // Exponentials per 16 evaluated by exp2_poly (FMA pipe) instead of MUFU ex2;
 // the replay is MUFU-bound (16384 exponentials per 512-cycle S^T MMA).
-constexpr int REPLAY_POLY = 4;
+constexpr int REPLAY_POLY = 2;
 
 template <int DP>
 struct ReplayCfg {
@@ -53,8 +53,8 @@ struct ReplayCfg {
   static constexpr int NCH = DP / 64;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_Q = TILE;
-  static constexpr int OFF_BIAS = OFF_Q + QST * TILE;     // float[4 warps][128]
-  static constexpr int OFF_MAP = OFF_BIAS + 4 * 128 * 4;  // uint32 bitmap of listed query blocks
+  static constexpr int OFF_BIAS = OFF_Q + QST * TILE;     // float[4 warps][2][128]
+  static constexpr int OFF_MAP = OFF_BIAS + 4 * 256 * 4;  // uint32 bitmap of listed query blocks
   static constexpr int MAP_WORDS = 256;                   // up to 8192 blocks
   static constexpr int OFF_BAR = OFF_MAP + MAP_WORDS * 4;
   // k_full, q_full[QST], q_empty[QST], s_full[2], s_free[2], drain
@@ -227,7 +227,6 @@ __global__ void __launch_bounds__(192, 2)
     const int key = kt * 128 + kr;
     const uint32_t lane_off = static_cast<uint32_t>(warp << 5) << 16;
     const float sc = p.sc;
-    float* wbias = sbias + warp * 128;
     double acc = 0.0;
     ReplayItems it;
     it.init(qt_lo, nqt, p.G, map);
@@ -238,75 +237,90 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int q = x.qt * 128 + static_cast<int>(lane) + 32 * u;
-        dst[u] = (q < p.N && q >= p.s_lo) ? st[q] : make_float2(0.f, 1.f);
+        dst[u] = (q < p.N && q >= p.s_lo) ? ld_global_f2_pinned(st + q) : make_float2(0.f, 1.f);
       }
     };
-    float2 ml_next[4];
-    if (it.valid()) load_stats(it, ml_next);
-    uint32_t i = 0;
-    bool ok = true;
-    for (; it.valid(); it.next(), ++i) {
-      const int sb = i & 1;
-      // Exponent bias of the item's 128 query columns; each warp keeps its own
-      // copy (lane l fills columns l, l+32, l+64, l+96) so the warpgroup needs
-      // no cross-warp barrier.  The row statistics of the next item are loaded
-      // here too, so their latency overlaps this item's reduction.
-      const float2 ml_cur[4] = {ml_next[0], ml_next[1], ml_next[2], ml_next[3]};
-      const int qcur = it.qt * 128;
-      {
-        ReplayItems nx = it;
-        nx.next();
-        if (nx.valid()) load_stats(nx, ml_next);
-      }
-      __syncwarp();
+    // Exponent bias of an item's 128 query columns, stored negated (the
+    // exponent is x*sc + bias) into one of this warp's two bias buffers;
+    // lane l fills columns l, l+32, l+64, l+96, so no cross-warp barrier.
+    auto write_bias = [&](int qt, const float2* ml, float* dst) {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int c = static_cast<int>(lane) + 32 * u;
-        const int q = qcur + c;
+        const int q = qt * 128 + c;
         float bias = INFINITY;
         if (q < p.N && q >= p.s_lo)
-          bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml_cur[u].x + log2f(ml_cur[u].y));
-        wbias[c] = -bias;  // stored negated: the exponent is x*sc + wbias
+          bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml[u].x + lg2_approx(ml[u].y));
+        dst[c] = -bias;
       }
-      __syncwarp();
+    };
+    // The bias of item i+1 is computed while item i is reduced (between its
+    // two 64-column halves); the statistics of item i+2 are prefetched then.
+    float2 ml_next[4];
+    if (it.valid()) {
+      float2 ml0[4];
+      load_stats(it, ml0);
+      write_bias(it.qt, ml0, sbias + warp * 256);
+      ReplayItems nx = it;
+      nx.next();
+      if (nx.valid()) load_stats(nx, ml_next);
+    }
+    uint32_t i = 0;
+    bool ok = true;
+    const uint64_t sc2 = f2_pack(sc, sc);
+    for (; it.valid(); it.next(), ++i) {
+      const int sb = i & 1;
+      const float* wbias = sbias + warp * 256 + sb * 128;
+      __syncwarp();  // this item's bias is written; the other buffer is free
       ok = warp_all(mbar_wait(&s_full[sb], (i >> 1) & 1, TO, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      float x[128];
-      {
-        uint32_t* xr = reinterpret_cast<uint32_t*>(x);
-        tmem_ld64_sync(tmem + lane_off + sb * 128, xr);
-        tmem_ld64_sync(tmem + lane_off + sb * 128 + 64, xr + 64);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
-      // exp2(x*sc - bias_q) summed over the 128 query columns: packed FP32x2
-      // FMA for the exponents, REPLAY_POLY of every 16 exponentials on the FMA
-      // pipe (exp2_poly) and the rest on MUFU, packed adds into four pair
-      // accumulators.  Diagonal tile: columns q < key are masked to -inf.
-      const float4* nb4 = reinterpret_cast<const float4*>(wbias);
-      const uint64_t sc2 = f2_pack(sc, sc);
       const bool diag = p.causal && it.qt == kt;
       uint64_t acc2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
+      // exp2(x*sc - bias_q) summed over the 128 query columns, in two halves
+      // of 64 (fewer live registers, more exponentials in flight): packed
+      // FP32x2 FMA for the exponents, REPLAY_POLY of every 16 on the FMA pipe
+      // (exp2_poly) and the rest on MUFU, packed adds into four pair
+      // accumulators.  Diagonal tile: columns q < key are masked to -inf.
 #pragma unroll
-      for (int c4 = 0; c4 < 32; ++c4) {
-        const float4 nb = nb4[c4];
+      for (int h = 0; h < 2; ++h) {
+        float x[64];
+        tmem_ld64_sync(tmem + lane_off + sb * 128 + h * 64, reinterpret_cast<uint32_t*>(x));
+        if (h == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[sb]);
+        }
+        const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 64);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = c4 * 4 + h * 2;
-          float a0, a1;
-          f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, h == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w)), a0,
-                    a1);
-          if (diag) {
-            a0 = (c >= kr) ? a0 : -INFINITY;
-            a1 = (c + 1 >= kr) ? a1 : -INFINITY;
+        for (int c4 = 0; c4 < 16; ++c4) {
+          const float4 nb = nb4[c4];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int c = c4 * 4 + hh * 2;
+            const int col = h * 64 + c;
+            float a0, a1;
+            f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, hh == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w)),
+                      a0, a1);
+            if (diag) {
+              a0 = (col >= kr) ? a0 : -INFINITY;
+              a1 = (col + 1 >= kr) ? a1 : -INFINITY;
+            }
+            const float p0 = ((c & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
+            const float p1 = (((c + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
+            acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
           }
-          const float p0 = ((c & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
-          const float p1 = (((c + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
-          acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
+        }
+        if (h == 0) {
+          ReplayItems nx = it;
+          nx.next();
+          if (nx.valid()) {
+            write_bias(nx.qt, ml_next, sbias + warp * 256 + (sb ^ 1) * 128);
+            nx.next();
+            if (nx.valid()) load_stats(nx, ml_next);
+          }
         }
       }
       float a0, a1, a2, a3, a4, a5, a6, a7;
