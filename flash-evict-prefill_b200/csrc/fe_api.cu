@@ -17,8 +17,10 @@
 #include <mutex>
 
 #include "fe_forward.cuh"
+#include "fe_gather.cuh"
 #include "fe_replay.cuh"
 #include "fe_select.cuh"
+#include "fe_snap.cuh"
 
 namespace {
 
@@ -70,9 +72,9 @@ int bind_device(const void* ptr, int* dev_out) {
 int padded_dim(int64_t d) { return d <= 64 ? 64 : (d <= 128 ? 128 : 0); }
 
 // TMA map over a [B, H, N, D] view with element strides s[4] (s[3] == 1),
-// box = 64 channels x 128 tokens, 128-byte swizzle, zero fill out of bounds.
+// box = 64 channels x box_rows tokens, 128-byte swizzle, zero fill out of bounds.
 int make_map(CUtensorMap* m, const void* ptr, const int64_t* s, int64_t B, int64_t H, int64_t N, int64_t D,
-             int dtype, const char* name) {
+             int dtype, const char* name, int box_rows = 128) {
   if (s[3] != 1) return fail(FE_STATUS_UNSUPPORTED, "%s: channel stride must be 1 (got %lld)", name, (long long)s[3]);
   if (reinterpret_cast<uintptr_t>(ptr) % 16)
     return fail(FE_STATUS_UNSUPPORTED, "%s: base pointer must be 16-byte aligned", name);
@@ -93,7 +95,8 @@ int make_map(CUtensorMap* m, const void* ptr, const int64_t* s, int64_t B, int64
     gstr[i] = (cuuint64_t)bytes;
     fallback = bytes * ext[i];
   }
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  if (box_rows < 1 || box_rows > 256) return fail(FE_STATUS_INVALID, "%s: bad TMA box", name);
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   auto enc = encode_fn();
   if (!enc) return fail(FE_STATUS_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -180,6 +183,125 @@ int launch_replay(const CUtensorMap& tq, const CUtensorMap& tk, const fe::Replay
   return FE_STATUS_OK;
 }
 
+// Describe a K/V gather: byte strides, destination rows and the widest chunk
+// (16/8/4/2/1 bytes) that divides the row size, every stride that is stepped
+// over and every base address.
+int make_gather_spec(fe::GatherSpec* g, const void* k, const int64_t* k_strides, const void* v,
+                     const int64_t* v_strides, void* k_out, void* v_out, int64_t batch, int64_t heads, int64_t tokens,
+                     int64_t budget, int64_t channels, int64_t elem_bytes) {
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return fail(FE_STATUS_INVALID, "elem_bytes must be 1, 2, 4 or 8");
+  if (channels < 1 || channels > (int64_t(1) << 20)) return fail(FE_STATUS_INVALID, "bad channels");
+  if (!k || !k_strides || !k_out) return fail(FE_STATUS_INVALID, "null pointer");
+  if ((v == nullptr) != (v_out == nullptr) || (v && !v_strides))
+    return fail(FE_STATUS_INVALID, "v and v_out must both be given or both be null");
+  const int64_t* strides[2] = {k_strides, v_strides};
+  const char* names[2] = {"k", "v"};
+  for (int t = 0; t < (v ? 2 : 1); ++t) {
+    if (strides[t][3] != 1) return fail(FE_STATUS_UNSUPPORTED, "%s: channel stride must be 1", names[t]);
+    for (int i = 0; i < 3; ++i)
+      if (strides[t][i] < 0) return fail(FE_STATUS_UNSUPPORTED, "%s: negative strides are not supported", names[t]);
+  }
+  memset(g, 0, sizeof(*g));
+  g->k_src = static_cast<const uint8_t*>(k);
+  g->v_src = static_cast<const uint8_t*>(v);
+  g->k_sb = k_strides[0] * elem_bytes;
+  g->k_sh = k_strides[1] * elem_bytes;
+  g->k_sn = k_strides[2] * elem_bytes;
+  if (v) {
+    g->v_sb = v_strides[0] * elem_bytes;
+    g->v_sh = v_strides[1] * elem_bytes;
+    g->v_sn = v_strides[2] * elem_bytes;
+  }
+  g->k_dst = static_cast<uint8_t*>(k_out);
+  g->v_dst = static_cast<uint8_t*>(v_out);
+  g->heads = heads;
+  g->tokens = tokens;
+  g->budget = budget;
+  g->row_bytes = (int)(channels * elem_bytes);
+  int64_t vals[12];
+  int nv = 0;
+  vals[nv++] = g->row_bytes;
+  vals[nv++] = (int64_t)reinterpret_cast<uintptr_t>(k);
+  vals[nv++] = (int64_t)reinterpret_cast<uintptr_t>(k_out);
+  if (batch > 1) vals[nv++] = g->k_sb;
+  if (heads > 1) vals[nv++] = g->k_sh;
+  if (tokens > 1) vals[nv++] = g->k_sn;
+  if (v) {
+    vals[nv++] = (int64_t)reinterpret_cast<uintptr_t>(v);
+    vals[nv++] = (int64_t)reinterpret_cast<uintptr_t>(v_out);
+    if (batch > 1) vals[nv++] = g->v_sb;
+    if (heads > 1) vals[nv++] = g->v_sh;
+    if (tokens > 1) vals[nv++] = g->v_sn;
+  }
+  int vec = 16;
+  for (int i = 0; i < nv; ++i)
+    while (vec > 1 && vals[i] % vec) vec >>= 1;
+  g->vec = vec;
+  return FE_STATUS_OK;
+}
+
+// SnapKV geometry: row groups of the packed window rows and the key chunks of
+// the statistics pass (a pure function of the shape, so the workspace size
+// query and the launch agree).
+struct SnapGeometry {
+  int w, w8, hpg, ppg, groups, nchunk, chunk_tiles, box;
+  int64_t workspace_floats;
+};
+
+int snap_geometry(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t window, SnapGeometry* g) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1 || tokens < 1 || q_heads % kv_heads)
+    return fail(FE_STATUS_INVALID, "bad shape");
+  if (window < 1) return fail(FE_STATUS_INVALID, "window must be a positive integer");
+  if (tokens > (int64_t(1) << 30)) return fail(FE_STATUS_UNSUPPORTED, "problem too large");
+  const int64_t G = q_heads / kv_heads;
+  g->w = (int)(window < tokens ? window : tokens);
+  g->w8 = (g->w + 7) / 8 * 8;
+  if (g->w8 <= 256) {
+    g->hpg = 256 / g->w8;
+    g->ppg = 0;
+    g->groups = (int)((G + g->hpg - 1) / g->hpg);
+    g->box = g->w8;
+  } else {
+    g->hpg = 0;
+    g->ppg = (g->w + 255) / 256;
+    g->groups = (int)(G * g->ppg);
+    g->box = 256;
+  }
+  const int64_t units = batch * kv_heads * g->groups;
+  const int64_t ntiles = (tokens + 127) / 128;
+  // About one statistics CTA per SM, at most 32 partials per row.
+  int64_t n = (148 + units - 1) / units;
+  if (n > 32) n = 32;
+  if (n > ntiles) n = ntiles;
+  if (n < 1) n = 1;
+  g->chunk_tiles = (int)((ntiles + n - 1) / n);
+  g->nchunk = (int)((ntiles + g->chunk_tiles - 1) / g->chunk_tiles);
+  g->workspace_floats = units * g->nchunk * 256 * 2;
+  if (units * g->nchunk > 0x7fffffff || batch * kv_heads * ntiles > 0x7fffffff)
+    return fail(FE_STATUS_UNSUPPORTED, "grid too large");
+  return FE_STATUS_OK;
+}
+
+template <bool BF16, int DP>
+int launch_snap(const CUtensorMap& tq, const CUtensorMap& tk, const fe::SnapParams& p, int64_t stats_items,
+                int64_t score_items, cudaStream_t stream) {
+  using C = fe::SnapCfg<DP>;
+  auto ka = fe::fe_snap_stats_kernel<BF16, DP>;
+  auto kb = fe::fe_snap_score_kernel<BF16, DP>;
+  int rc = set_smem(ka, C::A_SMEM);
+  if (rc) return rc;
+  rc = set_smem(kb, C::B_SMEM);
+  if (rc) return rc;
+  ka<<<dim3((unsigned)stats_items), dim3(C::THREADS), C::A_SMEM, stream>>>(tq, tk, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "snap statistics launch");
+  kb<<<dim3((unsigned)score_items), dim3(C::THREADS), C::B_SMEM, stream>>>(tq, tk, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "snap score launch");
+  return FE_STATUS_OK;
+}
+
 __global__ void fe_watchdog_kernel(uint64_t timeout_ns) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -206,7 +328,7 @@ __global__ void fe_exp2_selftest_kernel(const float* in, float* poly, float* muf
 
 extern "C" {
 
-int fe_abi_version(void) { return 1; }
+int fe_abi_version(void) { return 2; }
 
 int fe_selftest_exp2(const float* in, float* out_poly, float* out_mufu, int64_t n, void* stream) {
   g_err[0] = 0;
@@ -336,9 +458,14 @@ int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, con
   return dp == 64 ? launch_replay<false, 64>(tq, tk, p, items, s) : launch_replay<false, 128>(tq, tk, p, items, s);
 }
 
-int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
-                     int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, void* stream) {
-  g_err[0] = 0;
+}  // extern "C"
+
+namespace {
+
+// Selection launch; with g != nullptr the same launch also compacts K/V.
+int select_impl(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
+                int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, const fe::GatherSpec* g,
+                void* stream) {
   if (rows < 0 || tokens < 1) return fail(FE_STATUS_INVALID, "bad rows/tokens");
   if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
   if (recent < 0 || recent > budget) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
@@ -370,6 +497,9 @@ int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int6
   p.mask = mask;
   p.mask_evict = mask_evict ? 1 : 0;
   p.chunk = chunk;
+  p.gather = g ? 1 : 0;
+  if (g) p.g = *g;
+  else memset(&p.g, 0, sizeof(p.g));
   const int smem = (int)(chunk * 4);
   rc = set_smem(fe::fe_select_kernel, smem < 49152 ? 49152 : smem);
   if (rc) return rc;
@@ -395,6 +525,55 @@ int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int6
   return FE_STATUS_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
+                     int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, void* stream) {
+  g_err[0] = 0;
+  return select_impl(importance, rows, tokens, budget, recent, pool_kernel, indices, mask, mask_evict, nullptr,
+                     stream);
+}
+
+int fe_gather_tokens(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                     const int64_t* indices, void* k_out, void* v_out, int64_t batch, int64_t heads, int64_t tokens,
+                     int64_t budget, int64_t channels, int64_t elem_bytes, void* stream) {
+  g_err[0] = 0;
+  if (batch < 0 || heads < 0 || tokens < 1 || budget < 0) return fail(FE_STATUS_INVALID, "bad shape");
+  if (batch == 0 || heads == 0 || budget == 0) return FE_STATUS_OK;
+  if (!indices) return fail(FE_STATUS_INVALID, "null pointer");
+  fe::GatherSpec g;
+  int rc = make_gather_spec(&g, k, k_strides, v, v_strides, k_out, v_out, batch, heads, tokens, budget, channels,
+                            elem_bytes);
+  if (rc) return rc;
+  rc = bind_device(k, nullptr);
+  if (rc) return rc;
+  const int64_t per_row = (budget + fe::GATHER_POSITIONS - 1) / fe::GATHER_POSITIONS;
+  const int64_t blocks = per_row * batch * heads;
+  if (blocks > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
+  fe::fe_gather_kernel<<<(unsigned)blocks, fe::GATHER_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      g, indices, per_row);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gather launch");
+  return FE_STATUS_OK;
+}
+
+int fe_select_gather(const float* importance, int64_t batch, int64_t heads, int64_t tokens, int64_t budget,
+                     int64_t recent, int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict,
+                     const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides, void* k_out,
+                     void* v_out, int64_t channels, int64_t elem_bytes, void* stream) {
+  g_err[0] = 0;
+  if (batch < 0 || heads < 0 || tokens < 1) return fail(FE_STATUS_INVALID, "bad shape");
+  if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+  fe::GatherSpec g;
+  int rc = make_gather_spec(&g, k, k_strides, v, v_strides, k_out, v_out, batch, heads, tokens, budget, channels,
+                            elem_bytes);
+  if (rc) return rc;
+  return select_impl(importance, batch * heads, tokens, budget, recent, pool_kernel, indices, mask, mask_evict, &g,
+                     stream);
+}
+
 int fe_evict(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
              const int64_t* v_strides, void* out, float* importance, int64_t* indices, uint8_t* mask,
              float* row_stats, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels,
@@ -411,6 +590,81 @@ int fe_evict(const void* q, const int64_t* q_strides, const void* k, const int64
                         nullptr, 0, stream);
   if (rc) return rc;
   return fe_select_tokens(importance, batch * kv_heads, tokens, budget, recent, pool_kernel, indices, mask, 1, stream);
+}
+
+int fe_evict_compact(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
+                     const int64_t* v_strides, void* out, float* importance, int64_t* indices, uint8_t* mask,
+                     void* k_out, void* v_out, float* row_stats, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                     int64_t tokens, int64_t channels, int dtype, int causal, float scale, float recency_decay,
+                     int64_t observation_window, int value_weighted, int64_t budget, int64_t recent,
+                     int64_t pool_kernel, void* stream) {
+  if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+  if (recent < 0 || recent > budget) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
+  if (pool_kernel < 1 || pool_kernel % 2 != 1) return fail(FE_STATUS_INVALID, "pool_kernel must be a positive odd integer");
+  if (!k_out || !v_out) return fail(FE_STATUS_INVALID, "null pointer");
+  int rc = fe_attention_fwd(q, q_strides, k, k_strides, v, v_strides, out, row_stats, batch, q_heads, kv_heads, tokens,
+                            channels, dtype, causal, scale, nullptr, 0, stream);
+  if (rc) return rc;
+  rc = fe_replay_scores(q, q_strides, k, k_strides, v, v_strides, row_stats, importance, batch, q_heads, kv_heads,
+                        tokens, channels, dtype, causal, scale, recency_decay, observation_window, value_weighted,
+                        nullptr, 0, stream);
+  if (rc) return rc;
+  return fe_select_gather(importance, batch, kv_heads, tokens, budget, recent, pool_kernel, indices, mask, 1, k,
+                          k_strides, v, v_strides, k_out, v_out, channels, 2, stream);
+}
+
+int64_t fe_snap_workspace_floats(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t window) {
+  g_err[0] = 0;
+  SnapGeometry g;
+  if (snap_geometry(batch, q_heads, kv_heads, tokens, window, &g)) return -1;
+  return g.workspace_floats;
+}
+
+int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, float* scores,
+                   float* workspace, int64_t workspace_floats, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                   int64_t tokens, int64_t channels, int dtype, float scale, int64_t window, void* stream) {
+  g_err[0] = 0;
+  int rc = check_shapes(batch, q_heads, kv_heads, tokens, channels, dtype);
+  if (rc) return rc;
+  if (!q || !k || !scores || !workspace) return fail(FE_STATUS_INVALID, "null pointer");
+  if (!std::isfinite(scale)) return fail(FE_STATUS_INVALID, "scale must be finite");
+  SnapGeometry g;
+  if ((rc = snap_geometry(batch, q_heads, kv_heads, tokens, window, &g))) return rc;
+  if (workspace_floats < g.workspace_floats)
+    return fail(FE_STATUS_INVALID, "workspace too small: %lld floats needed", (long long)g.workspace_floats);
+  if (reinterpret_cast<uintptr_t>(workspace) % 8) return fail(FE_STATUS_INVALID, "workspace must be 8-byte aligned");
+  rc = bind_device(q, nullptr);
+  if (rc) return rc;
+  CUtensorMap tq, tk;
+  if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q", g.box))) return rc;
+  if ((rc = make_map(&tk, k, k_strides, batch, kv_heads, tokens, channels, dtype, "k"))) return rc;
+  fe::SnapParams p;
+  p.partial = reinterpret_cast<float2*>(workspace);
+  p.scores = scores;
+  p.B = (int)batch;
+  p.Hq = (int)q_heads;
+  p.Hkv = (int)kv_heads;
+  p.N = (int)tokens;
+  p.D = (int)channels;
+  p.G = (int)(q_heads / kv_heads);
+  p.w = g.w;
+  p.w8 = g.w8;
+  p.hpg = g.hpg;
+  p.ppg = g.ppg;
+  p.groups = g.groups;
+  p.nchunk = g.nchunk;
+  p.chunk_tiles = g.chunk_tiles;
+  p.sc = (float)((double)scale * 1.4426950408889634);
+  p.timeout_ns = (uint64_t)g_watchdog_ns;
+  const int64_t stats_items = batch * kv_heads * g.groups * g.nchunk;
+  const int64_t score_items = batch * kv_heads * ((tokens + 127) / 128);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int dp = padded_dim(channels);
+  if (dtype == FE_DTYPE_BF16)
+    return dp == 64 ? launch_snap<true, 64>(tq, tk, p, stats_items, score_items, s)
+                    : launch_snap<true, 128>(tq, tk, p, stats_items, score_items, s);
+  return dp == 64 ? launch_snap<false, 64>(tq, tk, p, stats_items, score_items, s)
+                  : launch_snap<false, 128>(tq, tk, p, stats_items, score_items, s);
 }
 
 int fe_device_status(int device, int clear, int* status_out) {

@@ -78,8 +78,6 @@ constexpr uint32_t FWD_REGS_LOW = 64;
 // Registers per thread the launch must provide for the split above.
 constexpr int FWD_REGS_NEEDED = (2 * 128 * FWD_REGS_HIGH + 128 * FWD_REGS_LOW + 383) / 384;
 
-__device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
-
 // One softmax exponential pass over a 128-column row: p = 2^(x*sce - m) with
 // packed FP32x2 FMAs for the arguments, MUFU ex2 for the exponentials (POLY of
 // every 16 on the FMA pipe instead), packed adds into four pair accumulators,
@@ -249,12 +247,12 @@ __global__ void __launch_bounds__(384, 1)
       }
       // Never leave the CTA with a TMA write in flight: wait for the last load
       // issued into each stage (already complete on the normal path).
-      mbar_wait(q_full, 0, TO, abort_flag);
+      mbar_wait_inflight(q_full, 0, TO);
       for (int s = 0; s < C::STAGES; ++s) {
         if (loads[s] == 0) continue;
         const uint32_t use = (loads[s] - 1) / 2;
-        mbar_wait(&k_full[s], use & 1, TO, abort_flag);
-        if (loads[s] % 2 == 0) mbar_wait(&v_full[s], use & 1, TO, abort_flag);
+        mbar_wait_inflight(&k_full[s], use & 1, TO);
+        if (loads[s] % 2 == 0) mbar_wait_inflight(&v_full[s], use & 1, TO);
       }
     }
   } else if (warp == 9) {
@@ -339,7 +337,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       // Drain: every MMA issued above has completed once this returns.
       umma_commit(drain);
-      mbar_wait(drain, 0, TO, abort_flag);
+      mbar_wait_inflight(drain, 0, TO);
     }
   }
   } else {

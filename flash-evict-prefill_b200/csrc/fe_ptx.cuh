@@ -76,7 +76,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase with the given parity to complete. Returns false if the
 // CTA-wide abort flag is raised or the watchdog limit passes; the latter also
-// records FE_STATUS_TIMEOUT.
+// records FE_STATUS_TIMEOUT and raises the abort flag.  With abort_flag ==
+// nullptr only the time limit ends the wait: used for the final waits on a
+// CTA's own TMA loads and MMAs in flight, which must land (or the limit pass)
+// before the CTA frees its TMEM and exits, also after an abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -85,14 +88,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 63u) == 0) {
-      if (*abort_flag) return false;
+      if (abort_flag != nullptr && *abort_flag) return false;
       if (globaltimer_ns() - t0 > timeout_ns) {
         raise_status(FE_STATUS_TIMEOUT);
-        *abort_flag = 1;
+        if (abort_flag != nullptr) *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// Final wait on work this CTA itself has in flight (see mbar_wait).
+__device__ __forceinline__ bool mbar_wait_inflight(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  return mbar_wait(bar, parity, timeout_ns, nullptr);
 }
 
 // --------------------------------------------------------------------- TMA --
@@ -336,6 +344,23 @@ __device__ __forceinline__ float lg2_approx(float x) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ bool warp_all(bool v) { return __all_sync(0xffffffffu, v); }
+
+// Round two FP32 values to the 16-bit input type and back (round to nearest
+// even), as a matmul that writes its result in the input dtype does.
+template <bool BF16>
+__device__ __forceinline__ void round_pair(float& a, float& b) {
+  const uint32_t r = pack2<BF16>(a, b);
+  if constexpr (BF16) {
+    a = __uint_as_float(r << 16);
+    b = __uint_as_float(r & 0xffff0000u);
+  } else {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(a), "=f"(b)
+        : "r"(r));
+  }
 }
 
 }  // namespace fe

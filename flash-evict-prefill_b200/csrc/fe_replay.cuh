@@ -183,9 +183,9 @@ __global__ void __launch_bounds__(192, 2)
             tma_load_4d(smem + C::OFF_Q + s * C::TILE + c * 16384, &tq, &q_full[s], c * 64, it.qt * 128, hq, b);
         }
         // Wait for the last load of each ring slot and for K before exiting.
-        mbar_wait(k_full, 0, TO, abort_flag);
+        mbar_wait_inflight(k_full, 0, TO);
         for (uint32_t i = (issued > C::QST ? issued - C::QST : 0); i < issued; ++i)
-          mbar_wait(&q_full[i % C::QST], (i / C::QST) & 1, TO, abort_flag);
+          mbar_wait_inflight(&q_full[i % C::QST], (i / C::QST) & 1, TO);
       }
     }
   } else if (warp == 5) {
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(192, 2)
           umma_commit(&q_empty[s]);
         }
         umma_commit(drain);
-        mbar_wait(drain, 0, TO, abort_flag);
+        mbar_wait_inflight(drain, 0, TO);
       }
     }
   } else {

@@ -20,10 +20,16 @@
 // passes whose histograms are merged through distributed shared memory.
 // Compaction walks each slice in index order (ballot/popc scans), so indices
 // come out already sorted; the cluster exchanges per-CTA counts for offsets.
+// Optionally the same launch compacts K and V into dense [rows, budget,
+// channels] buffers: once every CTA of the cluster has written its indices
+// (a cluster barrier orders them), CTA r copies the rows of output positions
+// [r*budget/C, (r+1)*budget/C), so the copy is balanced however unevenly the
+// kept tokens fall across the slices.
 #pragma once
 
 #include <cooperative_groups.h>
 
+#include "fe_gather.cuh"
 #include "fe_ptx.cuh"
 
 namespace fe {
@@ -38,6 +44,8 @@ struct SelectParams {
   uint8_t* mask;     // [rows, N]
   int mask_evict;
   int64_t chunk;     // slice length per CTA
+  int gather;        // nonzero: also copy the kept K/V rows (spec g)
+  GatherSpec g;
 };
 
 constexpr int SEL_THREADS = 1024;
@@ -78,6 +86,22 @@ __device__ __forceinline__ int block_flag_scan(bool flag, int* warp_sums, int* t
   return res;
 }
 
+// After the row's indices are complete (every CTA of the cluster calls this
+// once, after its last index store), copy the K/V rows of this CTA's share of
+// the output positions.  The cluster barrier (release/acquire at cluster
+// scope) makes the other CTAs' index stores visible; the gather reads the
+// indices through L2.
+__device__ __forceinline__ void gather_share(const SelectParams& p, cg::cluster_group& cluster, int64_t row,
+                                             const int64_t* out_idx, int C, int crank) {
+  cluster.sync();
+  const int64_t per = (p.budget + C - 1) / C;
+  const int64_t a = min(p.budget, static_cast<int64_t>(crank) * per);
+  const int64_t e = min(p.budget, a + per);
+  // two loads in flight per thread (1024 threads): the selection kernel runs
+  // at its 64-register limit
+  gather_rows<2>(p.g, row, out_idx, a, e - a, threadIdx.x, SEL_THREADS);
+}
+
 __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const SelectParams p) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
@@ -113,162 +137,164 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const SelectP
   }
   if (kk == 0) {
     for (int i = threadIdx.x; i < len; i += SEL_THREADS) out_mask[lo + i] = evict_v;
-    return;
-  }
-
-  // ---- keys of this slice (pooled if requested) ----
-  const bool pooled = p.pool > 1;
-  const int r = p.pool / 2;
-  for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
-    const int64_t gi = lo + i;
-    float x;
-    if (pooled) {
-      // Same accumulation as avg_pool1d: taps left to right inside the row,
-      // padding contributes nothing, divisor = kernel size.
-      float s = 0.f;
-      const int64_t a = gi - r > 0 ? gi - r : 0;
-      const int64_t e = gi + r + 1 < P ? gi + r + 1 : P;
-      for (int64_t t = a; t < e; ++t) s = __fadd_rn(s, imp[t]);
-      x = __fdiv_rn(s, static_cast<float>(p.pool));
-    } else {
-      x = imp[gi];
-    }
-    keys[i] = order_key(x);
-  }
-  for (int i = threadIdx.x; i < 512; i += SEL_THREADS) (&hist[0][0])[i] = 0;
-  __syncthreads();
-
-  // ---- radix select of the kk-th largest key over the whole cluster ----
-  uint32_t prefix = 0, pmask = 0;
-  uint32_t krem = static_cast<uint32_t>(kk);
-  for (int pass = 0; pass < 4; ++pass) {
-    const int buf = pass & 1;
-    const int shift = 24 - 8 * pass;
-    if (pass >= 2) {
-      // hist[buf] was last read by the cluster before the previous pass's
-      // cluster.sync(); clear it for reuse.
-      for (int i = threadIdx.x; i < 256; i += SEL_THREADS) hist[buf][i] = 0;
-      __syncthreads();
-    }
-    // Warp-aggregated counting: the lanes holding the same digit elect one
-    // of them to add the group's count (scores are often concentrated in a
-    // few digits, which would otherwise serialise the shared-memory atomics).
-    for (int base = 0; base < len; base += SEL_THREADS) {
-      const int i = base + threadIdx.x;
-      const uint32_t k = i < len ? keys[i] : 0u;
-      const bool match = (i < len) && ((k & pmask) == prefix);
-      const uint32_t digit = match ? ((k >> shift) & 255u) : 0x100u;
-      const uint32_t peers = __match_any_sync(0xffffffffu, digit);
-      if (match && (threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
-        atomicAdd(&hist[buf][digit], static_cast<uint32_t>(__popc(peers)));
-    }
-    cluster.sync();
-    if (threadIdx.x < 256) {
-      uint32_t s = 0;
-      for (int rr = 0; rr < C; ++rr) s += cluster.map_shared_rank(&hist[buf][0], rr)[threadIdx.x];
-      tot[threadIdx.x] = s;
-    }
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      // lane l owns digits [248-8l, 255-8l], scanned from the top.
-      const int lane = threadIdx.x;
-      uint32_t lsum = 0;
-#pragma unroll
-      for (int d = 0; d < 8; ++d) lsum += tot[255 - 8 * lane - d];
-      uint32_t incl = lsum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
+  } else {
+    // ---- keys of this slice (pooled if requested) ----
+    const bool pooled = p.pool > 1;
+    const int r = p.pool / 2;
+    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+      const int64_t gi = lo + i;
+      float x;
+      if (pooled) {
+        // Same accumulation as avg_pool1d: taps left to right inside the row,
+        // padding contributes nothing, divisor = kernel size.
+        float s = 0.f;
+        const int64_t a = gi - r > 0 ? gi - r : 0;
+        const int64_t e = gi + r + 1 < P ? gi + r + 1 : P;
+        for (int64_t t = a; t < e; ++t) s = __fadd_rn(s, imp[t]);
+        x = __fdiv_rn(s, static_cast<float>(p.pool));
+      } else {
+        x = imp[gi];
       }
-      uint32_t cum = incl - lsum;  // keys with a larger digit than this lane's range
-      if (cum < krem && krem <= incl) {
-#pragma unroll 1
-        for (int d = 0; d < 8; ++d) {
-          const int digit = 255 - 8 * lane - d;
-          const uint32_t c = tot[digit];
-          if (cum + c >= krem) {
-            sel_digit = static_cast<uint32_t>(digit);
-            sel_krem = krem - cum;
-            break;
+      keys[i] = order_key(x);
+    }
+    for (int i = threadIdx.x; i < 512; i += SEL_THREADS) (&hist[0][0])[i] = 0;
+    __syncthreads();
+
+    // ---- radix select of the kk-th largest key over the whole cluster ----
+    uint32_t prefix = 0, pmask = 0;
+    uint32_t krem = static_cast<uint32_t>(kk);
+    for (int pass = 0; pass < 4; ++pass) {
+      const int buf = pass & 1;
+      const int shift = 24 - 8 * pass;
+      if (pass >= 2) {
+        // hist[buf] was last read by the cluster before the previous pass's
+        // cluster.sync(); clear it for reuse.
+        for (int i = threadIdx.x; i < 256; i += SEL_THREADS) hist[buf][i] = 0;
+        __syncthreads();
+      }
+      // Warp-aggregated counting: the lanes holding the same digit elect one
+      // of them to add the group's count (scores are often concentrated in a
+      // few digits, which would otherwise serialise the shared-memory atomics).
+      for (int base = 0; base < len; base += SEL_THREADS) {
+        const int i = base + threadIdx.x;
+        const uint32_t k = i < len ? keys[i] : 0u;
+        const bool match = (i < len) && ((k & pmask) == prefix);
+        const uint32_t digit = match ? ((k >> shift) & 255u) : 0x100u;
+        const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+        if (match && (threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
+          atomicAdd(&hist[buf][digit], static_cast<uint32_t>(__popc(peers)));
+      }
+      cluster.sync();
+      if (threadIdx.x < 256) {
+        uint32_t s = 0;
+        for (int rr = 0; rr < C; ++rr) s += cluster.map_shared_rank(&hist[buf][0], rr)[threadIdx.x];
+        tot[threadIdx.x] = s;
+      }
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        // lane l owns digits [248-8l, 255-8l], scanned from the top.
+        const int lane = threadIdx.x;
+        uint32_t lsum = 0;
+  #pragma unroll
+        for (int d = 0; d < 8; ++d) lsum += tot[255 - 8 * lane - d];
+        uint32_t incl = lsum;
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += n;
+        }
+        uint32_t cum = incl - lsum;  // keys with a larger digit than this lane's range
+        if (cum < krem && krem <= incl) {
+  #pragma unroll 1
+          for (int d = 0; d < 8; ++d) {
+            const int digit = 255 - 8 * lane - d;
+            const uint32_t c = tot[digit];
+            if (cum + c >= krem) {
+              sel_digit = static_cast<uint32_t>(digit);
+              sel_krem = krem - cum;
+              break;
+            }
+            cum += c;
           }
-          cum += c;
         }
       }
+      __syncthreads();
+      prefix |= sel_digit << shift;
+      pmask |= 255u << shift;
+      krem = sel_krem;
+      __syncthreads();
     }
-    __syncthreads();
-    prefix |= sel_digit << shift;
-    pmask |= 255u << shift;
-    krem = sel_krem;
-    __syncthreads();
-  }
-  const uint32_t T = prefix;    // the kk-th largest key
-  const uint32_t need_eq = krem; // how many keys equal to T are kept (lowest indices)
+    const uint32_t T = prefix;    // the kk-th largest key
+    const uint32_t need_eq = krem; // how many keys equal to T are kept (lowest indices)
 
-  // ---- per-CTA counts, exchanged for offsets ----
-  int gt = 0, eq = 0;
-  for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
-    const uint32_t k = keys[i];
-    gt += k > T;
-    eq += k == T;
-  }
-  {
-    __shared__ int red[2][SEL_WARPS];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      gt += __shfl_xor_sync(0xffffffffu, gt, o);
-      eq += __shfl_xor_sync(0xffffffffu, eq, o);
+    // ---- per-CTA counts, exchanged for offsets ----
+    int gt = 0, eq = 0;
+    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+      const uint32_t k = keys[i];
+      gt += k > T;
+      eq += k == T;
     }
-    if (lane == 0) {
-      red[0][warp] = gt;
-      red[1][warp] = eq;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      long long tg = 0, te = 0;
-      for (int w = 0; w < SEL_WARPS; ++w) {
-        tg += red[0][w];
-        te += red[1][w];
+    {
+      __shared__ int red[2][SEL_WARPS];
+      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  #pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        gt += __shfl_xor_sync(0xffffffffu, gt, o);
+        eq += __shfl_xor_sync(0xffffffffu, eq, o);
       }
-      counts[0] = tg;
-      counts[1] = te;
+      if (lane == 0) {
+        red[0][warp] = gt;
+        red[1][warp] = eq;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        long long tg = 0, te = 0;
+        for (int w = 0; w < SEL_WARPS; ++w) {
+          tg += red[0][w];
+          te += red[1][w];
+        }
+        counts[0] = tg;
+        counts[1] = te;
+      }
     }
-  }
-  cluster.sync();
-  long long gt_before = 0, eq_before = 0;
-  for (int rr = 0; rr < crank; ++rr) {
-    const long long* rc = cluster.map_shared_rank(&counts[0], rr);
-    gt_before += rc[0];
-    eq_before += rc[1];
-  }
-  // Keep remote CTAs' shared memory alive until everyone has read it.
-  cluster.sync();
+    cluster.sync();
+    long long gt_before = 0, eq_before = 0;
+    for (int rr = 0; rr < crank; ++rr) {
+      const long long* rc = cluster.map_shared_rank(&counts[0], rr);
+      gt_before += rc[0];
+      eq_before += rc[1];
+    }
+    // Keep remote CTAs' shared memory alive until everyone has read it.
+    cluster.sync();
 
-  // ---- ordered compaction ----
-  long long run_gt = gt_before, run_eq = eq_before;
-  for (int base = 0; base < len; base += SEL_THREADS) {
-    const int i = base + threadIdx.x;
-    const bool in = i < len;
-    const uint32_t k = in ? keys[i] : 0u;
-    const bool is_eq = in && (k == T);
-    int tot_eq;
-    const int eq_rank = block_flag_scan(is_eq, warp_sums, &tot_eq);
-    const bool kept_eq = is_eq && (run_eq + eq_rank < static_cast<long long>(need_eq));
-    const bool kept = (in && k > T) || kept_eq;
-    int tot_kept;
-    const int pos = block_flag_scan(kept, warp_sums, &tot_kept);
-    // kept elements before this one over the whole row:
-    //   gt before the tile + kept-equal before the tile + in-tile prefix
-    const long long kept_eq_before = min(run_eq, static_cast<long long>(need_eq));
-    if (in) {
-      if (kept) out_idx[run_gt + kept_eq_before + pos] = lo + i;
-      out_mask[lo + i] = kept ? keep_v : evict_v;
+    // ---- ordered compaction ----
+    long long run_gt = gt_before, run_eq = eq_before;
+    for (int base = 0; base < len; base += SEL_THREADS) {
+      const int i = base + threadIdx.x;
+      const bool in = i < len;
+      const uint32_t k = in ? keys[i] : 0u;
+      const bool is_eq = in && (k == T);
+      int tot_eq;
+      const int eq_rank = block_flag_scan(is_eq, warp_sums, &tot_eq);
+      const bool kept_eq = is_eq && (run_eq + eq_rank < static_cast<long long>(need_eq));
+      const bool kept = (in && k > T) || kept_eq;
+      int tot_kept;
+      const int pos = block_flag_scan(kept, warp_sums, &tot_kept);
+      // kept elements before this one over the whole row:
+      //   gt before the tile + kept-equal before the tile + in-tile prefix
+      const long long kept_eq_before = min(run_eq, static_cast<long long>(need_eq));
+      if (in) {
+        if (kept) out_idx[run_gt + kept_eq_before + pos] = lo + i;
+        out_mask[lo + i] = kept ? keep_v : evict_v;
+      }
+      const long long kept_eq_after = min(run_eq + tot_eq, static_cast<long long>(need_eq));
+      run_gt += tot_kept - (kept_eq_after - kept_eq_before);
+      run_eq += tot_eq;
     }
-    const long long kept_eq_after = min(run_eq + tot_eq, static_cast<long long>(need_eq));
-    run_gt += tot_kept - (kept_eq_after - kept_eq_before);
-    run_eq += tot_eq;
   }
+
+  // ---- K/V compaction, an equal share of the output per CTA ----
+  if (p.gather) gather_share(p, cluster, row, out_idx, C, crank);
 }
 
 }  // namespace fe

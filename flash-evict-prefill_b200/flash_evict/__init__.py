@@ -2,8 +2,11 @@
 
 `prefill`, `evict` and `select_tokens` keep the reference's signatures
 (flash_evict/__init__.py:1-3 of the reference); the compute runs in the
-sm_100a native library bound by `_lib`.
+sm_100a native library bound by `_lib`.  `gather_tokens`,
+`select_and_gather` and `evict_compact` (flash_evict.compact) add the KV
+compaction the reference's adapters perform after selection.
 """
 from .prefill import prefill, evict, select_tokens
+from .compact import gather_tokens, select_and_gather, evict_compact
 
-__all__ = ["prefill", "evict", "select_tokens"]
+__all__ = ["prefill", "evict", "select_tokens", "gather_tokens", "select_and_gather", "evict_compact"]

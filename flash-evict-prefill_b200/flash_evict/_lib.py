@@ -17,6 +17,7 @@ STATUS_INVALID = 1
 STATUS_UNSUPPORTED = 2
 STATUS_CUDA = 3
 STATUS_TIMEOUT = 4
+STATUS_BAD_INDEX = 5
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
 QUERY_BLOCK = 256
@@ -26,6 +27,7 @@ _STATUS_NAMES = {
     STATUS_UNSUPPORTED: "unsupported",
     STATUS_CUDA: "CUDA error",
     STATUS_TIMEOUT: "device watchdog timeout",
+    STATUS_BAD_INDEX: "gather index out of range",
 }
 
 _I64P = ctypes.POINTER(ctypes.c_int64)
@@ -43,6 +45,14 @@ SIGNATURES = {
     "fe_select_tokens": (_INT, [_VP, _I64, _I64, _I64, _I64, _I64, _VP, _VP, _INT, _VP]),
     "fe_evict": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _VP, _I64, _I64, _I64, _I64,
                         _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
+    "fe_gather_tokens": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _VP]),
+    "fe_select_gather": (_INT, [_VP, _I64, _I64, _I64, _I64, _I64, _I64, _VP, _VP, _INT, _VP, _I64P, _VP, _I64P,
+                                _VP, _VP, _I64, _I64, _VP]),
+    "fe_evict_compact": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64,
+                                _I64, _I64, _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
+    "fe_snap_workspace_floats": (_I64, [_I64, _I64, _I64, _I64, _I64]),
+    "fe_snap_scores": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _INT, _F32,
+                              _I64, _VP]),
     "fe_evict_noalloc": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _I64, _I64, _I64,
                                 _I64, _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
     "fe_device_status": (_INT, [_INT, _INT, ctypes.POINTER(_INT)]),

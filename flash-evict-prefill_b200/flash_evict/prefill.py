@@ -196,11 +196,13 @@ def evict(q, k, v, budget, *, recent=0, reserved_recent=None, pool_kernel=1, **k
     return _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, None, kwargs)
 
 
-def _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, marks, kwargs):
+def _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, marks, kwargs, compact=False):
     """Body of `evict` (reference prefill.py:173-180): prefill then selection,
     with the eviction mask written directly by the selection kernel.
     `marks`, when given, is called with a stage name before the first launch
-    and after each launch (bench.py places CUDA events there)."""
+    and after each launch (bench.py places CUDA events there).  With
+    compact=True the selection launch also gathers the kept K/V rows and two
+    more tensors are returned (flash_evict.compact.evict_compact)."""
     if kwargs.get("score") is False:
         raise ValueError("evict requires importance scoring")
     kwargs = dict(kwargs)
@@ -237,9 +239,19 @@ def _evict_impl(q, k, v, budget, recent, reserved_recent, pool_kernel, marks, kw
                 value_weighted)
         if marks:
             marks("replay")
-        _lib.check(lib.fe_select_tokens(
-            importance.data_ptr(), b * hk, n, budget, recent, pool_kernel, indices.data_ptr(),
-            eviction_mask.data_ptr(), 1, _stream(q.device)))
+        if compact:
+            k_kept = torch.empty((b, hk, budget, d), dtype=k.dtype, device=q.device)
+            v_kept = torch.empty_like(k_kept)
+            _lib.check(lib.fe_select_gather(
+                importance.data_ptr(), b, hk, n, budget, recent, pool_kernel, indices.data_ptr(),
+                eviction_mask.data_ptr(), 1, kv.data_ptr(), _lib.strides(kv), vv.data_ptr(), _lib.strides(vv),
+                k_kept.data_ptr(), v_kept.data_ptr(), d, kv.element_size(), _stream(q.device)))
+        else:
+            _lib.check(lib.fe_select_tokens(
+                importance.data_ptr(), b * hk, n, budget, recent, pool_kernel, indices.data_ptr(),
+                eviction_mask.data_ptr(), 1, _stream(q.device)))
         if marks:
             marks("select")
+    if compact:
+        return out, importance, indices, eviction_mask, k_kept, v_kept
     return out, importance, indices, eviction_mask

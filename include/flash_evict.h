@@ -44,6 +44,7 @@ extern "C" {
 #define FE_STATUS_UNSUPPORTED 2 /* valid request outside what the kernels do    */
 #define FE_STATUS_CUDA 3        /* a CUDA runtime/driver call failed            */
 #define FE_STATUS_TIMEOUT 4     /* a device wait exceeded the watchdog limit    */
+#define FE_STATUS_BAD_INDEX 5   /* a gather index was outside [0, tokens)       */
 
 #define FE_DTYPE_F16 0
 #define FE_DTYPE_BF16 1
@@ -107,6 +108,59 @@ FE_API int fe_evict(const void* q, const int64_t* q_strides, const void* k, cons
              int64_t observation_window, int value_weighted, int64_t budget, int64_t recent,
              int64_t pool_kernel, void* stream);
 
+/* KV compaction gather.  Replaces `gather_tokens(x, indices)` from the
+ * adapters' kv_distill dependency, applied to K and V after selection
+ * (flash_evict/kv_distill_adapter.py:38-39, flash_evict/streaming_adapter.py:86,
+ * flash_evict/quality_adapter.py:109-110; README.md:31 gives its meaning as
+ * x.gather(2, indices[..., None].expand(-1, -1, -1, channels))):
+ *   k_out[b,h,j,:] = k[b,h,indices[b,h,j],:]   (and the same for v).
+ * k, v: [batch, heads, tokens, channels] with element strides (channel
+ * stride 1, other strides >= 0), elem_bytes bytes per element (1, 2, 4, 8);
+ * v and v_out may both be NULL to gather K only.  indices: contiguous int64
+ * [batch, heads, budget], any order.  k_out, v_out: contiguous
+ * [batch, heads, budget, channels].  An index outside [0, tokens) does not
+ * fault: its destination row is zero-filled and FE_STATUS_BAD_INDEX is raised
+ * in the device status word (fe_device_status). */
+FE_API int fe_gather_tokens(const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            const int64_t* indices, void* k_out, void* v_out, int64_t batch, int64_t heads,
+                            int64_t tokens, int64_t budget, int64_t channels, int64_t elem_bytes, void* stream);
+/* fe_select_tokens and fe_gather_tokens in one launch: rows = batch*heads of
+ * importance are selected exactly as by fe_select_tokens, and each CTA of the
+ * selection copies the K/V rows of the indices it produced into k_out/v_out
+ * (layouts as in fe_gather_tokens).  Replaces the compress step of the
+ * adapters, `select_tokens` followed by two `gather_tokens`
+ * (flash_evict/kv_distill_adapter.py:35-39). */
+FE_API int fe_select_gather(const float* importance, int64_t batch, int64_t heads, int64_t tokens, int64_t budget,
+                            int64_t recent, int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict,
+                            const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                            void* k_out, void* v_out, int64_t channels, int64_t elem_bytes, void* stream);
+/* fe_evict followed by the compaction of K and V into k_out/v_out
+ * ([batch, kv_heads, budget, channels], dtype of the inputs), the selection
+ * and the gather sharing one launch.  README.md:27-31 (evict, then gather). */
+FE_API int fe_evict_compact(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                            const void* v, const int64_t* v_strides, void* out, float* importance, int64_t* indices,
+                            uint8_t* mask, void* k_out, void* v_out, float* row_stats, int64_t batch,
+                            int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype,
+                            int causal, float scale, float recency_decay, int64_t observation_window,
+                            int value_weighted, int64_t budget, int64_t recent, int64_t pool_kernel, void* stream);
+/* SnapKV observation-window scores, the reference's comparison baseline.
+ * Replaces `snap_scores` (flash_evict/baselines.py:12-26): with
+ * w = min(window, tokens), for the last w query rows of every query head
+ *   p = softmax(round(Q_w K^T) * scale, causal)   (FP32)
+ * where round() is the rounding of the FP32 dot products to `dtype` that the
+ * reference's native-dtype matmul performs; p is summed over the w rows and
+ * averaged over the G = q_heads/kv_heads query heads of each KV head:
+ * scores: FP32 [batch, kv_heads, tokens], contiguous.  Two launches (split
+ * row statistics, then a key-stationary scoring pass); the w x tokens matrix
+ * is never stored.  workspace: at least fe_snap_workspace_floats(...) floats,
+ * 8-byte aligned, contents irrelevant.  Q/K layout rules as for
+ * fe_attention_fwd; channels <= 128. */
+FE_API int64_t fe_snap_workspace_floats(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens,
+                                        int64_t window);
+FE_API int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                          float* scores, float* workspace, int64_t workspace_floats, int64_t batch, int64_t q_heads,
+                          int64_t kv_heads, int64_t tokens, int64_t channels, int dtype, float scale, int64_t window,
+                          void* stream);
 /* evict() without any device allocation: like fe_evict, but the row-statistics
  * scratch lives in a fixed array inside this library instead of a
  * caller-provided workspace.  No counterpart in the reference (which always

@@ -209,6 +209,74 @@ def select_tokens(importance, budget, *, recent=0, reserved_recent=None, pool_ke
     return idx.reshape(lead + (budget,)), keep.reshape(imp.shape)
 
 
+def gather_tokens(x, indices):
+    """KV compaction: x[b, h, indices[b, h, j], :] (README.md:31,
+    `k.gather(2, indices[..., None].expand(-1, -1, -1, k.shape[-1]))`; the
+    adapters call it through kv_distill's gather_tokens at
+    kv_distill_adapter.py:38-39, streaming_adapter.py:86,
+    quality_adapter.py:109-110)."""
+    x = np.asarray(x)
+    idx = np.asarray(indices, dtype=np.int64)
+    return np.take_along_axis(x, idx[..., None], axis=2)
+
+
+def round_to_dtype(x, dtype_name):
+    """Round float32 values to float16/bfloat16 and back, round to nearest
+    even (what a matmul that writes its output in that dtype does)."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype_name == "float16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype_name == "bfloat16":
+        u = x.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+        return r.view(np.float32)
+    return x
+
+
+def snap_scores(q, k, window=32, dtype_name="bfloat16"):
+    """SnapKV observation-window scores (baselines.py:12-26).
+
+    q [B,Hq,N,D], k [B,Hkv,N,D] hold the fp16/bf16 input values as floats.
+    logits = round_to_dtype(q[:, :, -w:] @ k^T) (the reference's matmul runs in
+    the input dtype), then * D**-0.5 in float32, keys after the query's
+    position masked, softmax over the keys (float64 here), summed over the w
+    window rows and averaged over the G query heads of each KV head.  One
+    query head at a time, so memory stays at w x N.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    b, h, n, d = q.shape
+    hk = k.shape[1]
+    g = h // hk
+    w = min(window, n)
+    qpos = np.arange(n - w, n)
+    masked = np.arange(n)[None, :] > qpos[:, None]
+    scale = np.float32(d ** -0.5)
+    out = np.zeros((b, hk, n), dtype=np.float64)
+    for bi in range(b):
+        for hi in range(h):
+            logits = q[bi, hi, n - w:] @ k[bi, hi // g].T
+            logits = round_to_dtype(logits.astype(np.float32), dtype_name) * scale
+            logits = np.where(masked, -np.inf, logits.astype(np.float64))
+            p = np.exp(logits - logits.max(-1, keepdims=True))
+            p /= p.sum(-1, keepdims=True)
+            out[bi, hi // g] += p.sum(0)
+    return (out / g).astype(np.float32)
+
+
+def snap_select(scores, budget, window=32, kernel=5):
+    """baselines.py:29-43: all tokens when N <= budget, else the window
+    suffix plus the top of the average-pooled past (select_tokens with
+    recent = min(window, N, budget-1) and pool_kernel = kernel)."""
+    scores = np.asarray(scores)
+    n = scores.shape[-1]
+    if n <= budget:
+        idx = np.broadcast_to(np.arange(n), scores.shape[:-1] + (n,))
+        return idx, np.ones(scores.shape, dtype=bool)
+    window = min(window, n, budget - 1)
+    return select_tokens(scores, budget, recent=window, pool_kernel=kernel)
+
+
 def uniform_analytic(v, groups):
     """Q = K = 0, causal: P[q,k] = 1/(q+1) for k <= q.  Returns (out, importance)
     for value-weighted scoring (tests/test_prefill.py:88-102 of the reference).

@@ -34,6 +34,25 @@ def load_case(name):
     return rec
 
 
+def snap_cases():
+    """The SnapKV fixtures (tests/golden/snap.npz, from the reference's
+    baselines.snap_scores / snap_select): list of dicts with torch q/k (q
+    zero outside the window rows, which do not enter the scores)."""
+    z = np.load(os.path.join(GOLDEN, "snap.npz"), allow_pickle=False)
+    cases = []
+    for j in range(int(z["ncases"])):
+        dtype = DTYPES[str(z[f"s{j}_dtype"])]
+        b, h, hk, n, d = (int(x) for x in z[f"s{j}_shape"])
+        window, budget = (int(x) for x in z[f"s{j}_args"])
+        qwin = from_bits(z[f"s{j}_qwin"], dtype)
+        q = torch.zeros((b, h, n, d), dtype=dtype)
+        q[:, :, n - qwin.shape[2]:] = qwin
+        cases.append(dict(name=str(z[f"s{j}_name"]), dtype=dtype, dtype_name=str(z[f"s{j}_dtype"]), q=q,
+                          k=from_bits(z[f"s{j}_k"], dtype), window=window, budget=budget,
+                          scores=z[f"s{j}_scores"], idx=z[f"s{j}_idx"], keep=z[f"s{j}_keep"]))
+    return cases
+
+
 def strided_like_model(t):
     """Same values in the adapters' layout: a [B,H,N,D] view of a [B,N,H,D]
     buffer (noncontiguous strides)."""

@@ -13,8 +13,12 @@ tests/golden/*.npz:
   triton_interp.npz        the reference's own Triton kernel `_prefill` run by
                            the Triton CPU interpreter (fp16 only; the
                            interpreter mishandles bf16), output and importance
+  snap.npz                 the reference's flash_evict/baselines.py:snap_scores
+                           and snap_select (torch, CPU) on seeded q/k, windows
+                           inside one 256-row group, several groups, and a
+                           window longer than 256 rows
 
-Usage: python tests/golden/make_golden.py --reference /path/to/reference
+Usage: python tests/golden/make_golden.py --reference /path/to/reference [--only NAME ...]
 """
 import argparse
 import math
@@ -111,6 +115,44 @@ def selection_fixtures():
     print("wrote selection")
 
 
+# (name, B, Hq, Hkv, N, D, dtype, window, q_scale, budget)
+SNAP_CASES = [
+    ("ref_test_w32", 1, 6, 2, 137, 32, torch.bfloat16, 32, 1.0, 48),     # tests/test_baselines.py:11-14 shape
+    ("ref_test_full", 1, 6, 2, 137, 32, torch.bfloat16, 137, 1.0, 48),  # tests/test_baselines.py:21
+    ("f16_g2_w32", 1, 4, 2, 300, 64, torch.float16, 32, 1.0, 30),
+    ("bf16_g4_w48_b2", 2, 8, 2, 200, 64, torch.bfloat16, 48, 1.0, 20),
+    ("bf16_g7_w32_d128", 1, 28, 4, 400, 128, torch.bfloat16, 32, 1.0, 40),
+    ("bf16_w300_pieces", 1, 2, 1, 600, 64, torch.bfloat16, 300, 1.0, 60),
+    ("f16_window_gt_n", 1, 4, 1, 100, 64, torch.float16, 500, 1.0, 10),
+    ("bf16_x8_logits", 1, 4, 2, 260, 64, torch.bfloat16, 40, 8.0, 26),
+    ("f16_n1", 1, 2, 1, 1, 16, torch.float16, 32, 1.0, 1),
+]
+
+
+def snap_fixtures():
+    from flash_evict.baselines import snap_scores, snap_select
+    rec = {}
+    for j, (name, b, h, hk, n, d, dtype, window, qs, budget) in enumerate(SNAP_CASES):
+        g = torch.Generator().manual_seed(3000 + j)
+        q = (torch.randn((b, h, n, d), generator=g) * qs).to(dtype)
+        k = torch.randn((b, hk, n, d), generator=g).to(dtype)
+        scores = snap_scores(q, k, window)
+        idx, keep = snap_select(scores, budget, window)
+        rec[f"s{j}_name"] = np.array(name)
+        # only the window rows of q enter the scores; the rest are not stored
+        w = min(window, n)
+        rec[f"s{j}_qwin"], rec[f"s{j}_k"] = bits(q[:, :, n - w:]), bits(k)
+        rec[f"s{j}_shape"] = np.array([b, h, hk, n, d])
+        rec[f"s{j}_dtype"] = np.array(str(dtype).split(".")[-1])
+        rec[f"s{j}_args"] = np.array([window, budget])
+        rec[f"s{j}_scores"] = scores.numpy()
+        rec[f"s{j}_idx"] = idx.numpy()
+        rec[f"s{j}_keep"] = keep.numpy()
+    rec["ncases"] = np.array(len(SNAP_CASES))
+    np.savez_compressed(os.path.join(HERE, "snap.npz"), **rec)
+    print("wrote snap")
+
+
 INTERP_SNIPPET = r"""
 import sys, math, numpy as np, torch
 sys.path.insert(0, sys.argv[1])
@@ -151,12 +193,20 @@ def triton_fixture(reference):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of anishesg/flash-evict-prefill")
+    ap.add_argument("--only", nargs="*", choices=["materialized", "selection", "triton", "snap"],
+                    help="regenerate only these fixture files")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     torch.set_num_threads(8)
-    materialized_fixtures(args.reference)
-    selection_fixtures()
-    triton_fixture(args.reference)
+    only = set(args.only or ["materialized", "selection", "triton", "snap"])
+    if "materialized" in only:
+        materialized_fixtures(args.reference)
+    if "selection" in only:
+        selection_fixtures()
+    if "triton" in only:
+        triton_fixture(args.reference)
+    if "snap" in only:
+        snap_fixtures()
 
 
 if __name__ == "__main__":

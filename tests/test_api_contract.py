@@ -45,6 +45,7 @@ def test_header_constants_match_binding():
     assert int(defs["FE_STATUS_UNSUPPORTED"]) == _lib.STATUS_UNSUPPORTED
     assert int(defs["FE_STATUS_CUDA"]) == _lib.STATUS_CUDA
     assert int(defs["FE_STATUS_TIMEOUT"]) == _lib.STATUS_TIMEOUT
+    assert int(defs["FE_STATUS_BAD_INDEX"]) == _lib.STATUS_BAD_INDEX
     assert int(defs["FE_DTYPE_F16"]) == _lib.DTYPE_F16
     assert int(defs["FE_DTYPE_BF16"]) == _lib.DTYPE_BF16
     assert int(defs["FE_QUERY_BLOCK"]) == _lib.QUERY_BLOCK
@@ -52,17 +53,30 @@ def test_header_constants_match_binding():
 
 def test_library_host_calls_without_gpu():
     lib = _lib.load()
-    assert lib.fe_abi_version() == 1
+    assert lib.fe_abi_version() == 2
     # argument checks run on the host before any device work
     rc = lib.fe_select_tokens(None, 1, 10, 0, 0, 1, None, None, 1, None)
     assert rc == _lib.STATUS_INVALID
     assert b"budget" in lib.fe_last_error()
     rc = lib.fe_select_tokens(None, 1, 10, 4, 0, 2, None, None, 1, None)
     assert rc == _lib.STATUS_INVALID and b"pool_kernel" in lib.fe_last_error()
+    st = (ctypes.c_int64 * 4)(8, 8, 8, 2)
+    fake = 256  # never dereferenced: the argument checks fail first
+    rc = lib.fe_gather_tokens(fake, st, None, None, fake, fake, None, 1, 1, 8, 4, 8, 3, None)
+    assert rc == _lib.STATUS_INVALID and b"elem_bytes" in lib.fe_last_error()
+    rc = lib.fe_gather_tokens(fake, st, fake, st, fake, fake, None, 1, 1, 8, 4, 8, 2, None)
+    assert rc == _lib.STATUS_INVALID and b"both" in lib.fe_last_error()
+    rc = lib.fe_gather_tokens(fake, st, None, None, fake, fake, None, 1, 1, 8, 4, 8, 2, None)
+    assert rc == _lib.STATUS_UNSUPPORTED and b"channel stride" in lib.fe_last_error()
+    rc = lib.fe_gather_tokens(None, st, None, None, None, None, None, 1, 1, 8, 0, 8, 2, None)
+    assert rc == _lib.STATUS_OK  # nothing to gather
+    rc = lib.fe_select_gather(None, 1, 1, 10, 11, 0, 1, None, None, 1, None, st, None, st, None, None, 8, 2, None)
+    assert rc == _lib.STATUS_INVALID and b"budget" in lib.fe_last_error()
 
 
 def test_public_api_surface():
-    assert flash_evict.__all__ == ["prefill", "evict", "select_tokens"]
+    assert flash_evict.__all__[:3] == ["prefill", "evict", "select_tokens"]
+    assert set(flash_evict.__all__[3:]) == {"gather_tokens", "select_and_gather", "evict_compact"}
     import inspect
     sig = inspect.signature(prefill)
     assert list(sig.parameters) == ["q", "k", "v", "causal", "value_weighted", "score", "scale", "block_q",

@@ -1,0 +1,145 @@
+"""SnapKV baseline on the GPU: snap_scores against the reference's own
+outputs (tests/golden/snap.npz) and the oracle, snap_select exactness,
+flash_snap restating the reference's tests/test_baselines.py:9-25, and the
+size-independent mass identity at full size.
+
+Tolerance of snap_scores: the reference rounds each window logit to the
+input dtype after an FP32 dot product; the tensor cores may sum those
+products in another order, so a logit that lies on a rounding boundary can
+land one fp16/bf16 step away (about 1 logit in 10^4).  One such step moves
+that probability by at most |logit| * 2^-8 * scale (a few 1e-3 relative).
+So: 99.9 % of scores within 1e-4 relative, every score within 2e-2
+relative (+1e-6 absolute); the mass identity sum_k score = w holds to 1e-4.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from common import snap_cases
+from flash_evict import _lib
+from flash_evict.baselines import flash_attention, flash_snap, snap_scores, snap_select
+from oracle import restate as O
+
+pytestmark = pytest.mark.gpu
+
+
+def check_scores(got, ref, name=""):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    rel = np.abs(got - ref) / (np.abs(ref) + 1e-6)
+    assert np.quantile(rel, 0.999) < 1e-4, (name, np.quantile(rel, 0.999))
+    assert rel.max() < 2e-2, (name, rel.max())
+
+
+@pytest.mark.parametrize("case", snap_cases(), ids=lambda c: c["name"])
+def test_snap_scores_match_reference_fixtures(case):
+    q, k = case["q"].cuda(), case["k"].cuda()
+    s = snap_scores(q, k, case["window"])
+    assert s.dtype == torch.float32 and s.shape == (k.shape[0], k.shape[1], k.shape[2])
+    check_scores(s.cpu().numpy(), case["scores"], case["name"])
+    # selection is exact given the scores
+    idx, keep = snap_select(torch.from_numpy(case["scores"]).cuda(), case["budget"], case["window"])
+    np.testing.assert_array_equal(idx.cpu().numpy(), case["idx"])
+    np.testing.assert_array_equal(keep.cpu().numpy(), case["keep"])
+
+
+def test_window_baseline_reference_test():
+    # restates tests/test_baselines.py:9-21 (the kv_distill comparison at
+    # :22-25 needs that external package and is not reproducible here)
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(1, 6, 137, 32, generator=g).to(torch.bfloat16).cuda()
+    k = torch.randn(1, 2, 137, 32, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(1, 2, 137, 32, generator=g).to(torch.bfloat16).cuda()
+    out, scores, indices, mask = flash_snap(q, k, v, 48, 32)
+    expected, _ = O.materialized(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy())
+    np.testing.assert_allclose(out.float().cpu().numpy(), expected, atol=.015, rtol=.015)
+    assert (~mask).sum(-1).eq(48).all()
+    assert not mask[..., -32:].any()
+    _, hh = O.materialized(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                           value_weighted=False)
+    np.testing.assert_allclose(snap_scores(q, k, 137).cpu().numpy(), hh / 3, atol=.025, rtol=.005)
+    np.testing.assert_array_equal(indices.cpu().numpy(),
+                                  O.snap_select(scores.cpu().numpy(), 48, 32)[0])
+
+
+@pytest.mark.parametrize("shape", [
+    # B, Hq, Hkv, N, D, dtype, window
+    (1, 28, 4, 32768, 128, torch.bfloat16, 32),   # Qwen-style GQA 7:1 at 32K
+    (1, 32, 8, 8192, 128, torch.float16, 128),
+    (2, 8, 8, 3000, 64, torch.bfloat16, 32),      # MHA, two batch elements
+    (1, 16, 2, 5000, 80, torch.float16, 100),     # padded head dim, several groups
+    (1, 4, 1, 2000, 128, torch.bfloat16, 700),    # window longer than 256 rows
+])
+def test_snap_scores_vs_oracle(shape):
+    b, h, hk, n, d, dtype, w = shape
+    g = torch.Generator().manual_seed(n + d)
+    qb = torch.randn(b, n, h, d, generator=g).to(dtype)
+    q = qb.cuda().transpose(1, 2)  # adapters' [B, N, H, D] strides
+    k = torch.randn(b, hk, n, d, generator=g).to(dtype).cuda()
+    s = snap_scores(q, k, w).cpu().numpy()
+    ref = O.snap_scores(q.float().cpu().numpy(), k.float().cpu().numpy(), w, str(dtype).split(".")[-1])
+    check_scores(s, ref, str(shape))
+    np.testing.assert_allclose(s.sum(-1), min(w, n), rtol=1e-4)
+    budget = max(w + 1, n // 10)
+    idx, keep = snap_select(torch.from_numpy(s).cuda(), budget, w)
+    ridx, rkeep = O.snap_select(s, budget, w)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+    np.testing.assert_array_equal(keep.cpu().numpy(), rkeep)
+
+
+def test_snap_mass_identity_full_size():
+    # every window row's softmax sums to 1: sum_k score = w, independent of N
+    g = torch.Generator().manual_seed(9)
+    q = (torch.randn(1, 32, 131072, 128, generator=g) * 2).to(torch.bfloat16).cuda()
+    k = torch.randn(1, 8, 131072, 128, generator=g).to(torch.bfloat16).cuda()
+    s = snap_scores(q, k, 32)
+    assert torch.isfinite(s).all() and (s >= 0).all()
+    torch.testing.assert_close(s.double().sum(-1), torch.full((1, 8), 32., dtype=torch.float64).cuda(),
+                               rtol=1e-4, atol=0)
+    # the last token sees only itself in the last row: p = 1 there, 0 elsewhere
+    assert s[..., -1].min() > 0
+
+
+def test_snap_select_small_and_full_budget():
+    s = torch.rand(2, 3, 40).cuda()
+    idx, keep = snap_select(s, 40)
+    assert idx.shape == (2, 3, 40) and keep.all()
+    idx, keep = snap_select(s, 100)
+    assert idx.shape == (2, 3, 40) and torch.equal(idx[0, 0], torch.arange(40).cuda())
+    idx, keep = snap_select(s, 5, window=32)  # window clamps to budget-1
+    ridx, rkeep = O.snap_select(s.cpu().numpy(), 5, 32)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)
+    np.testing.assert_array_equal(keep.cpu().numpy(), rkeep)
+    with pytest.raises(ValueError):
+        snap_select(s, 10, kernel=4)
+
+
+def test_flash_attention_matches_oracle():
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(1, 8, 700, 64, generator=g).to(torch.float16).cuda()
+    k = torch.randn(1, 2, 700, 64, generator=g).to(torch.float16).cuda()
+    v = torch.randn(1, 2, 700, 64, generator=g).to(torch.float16).cuda()
+    out = flash_attention(q, k, v)
+    ref, _ = O.materialized(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy())
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=2e-3, rtol=6e-3)
+
+
+def test_c_abi_snap_workspace_contract():
+    lib = _lib.load()
+    assert lib.fe_snap_workspace_floats(1, 28, 4, 32768, 32) > 0
+    assert lib.fe_snap_workspace_floats(1, 28, 4, 32768, 0) < 0
+    q = torch.randn(1, 4, 300, 64, dtype=torch.bfloat16, device="cuda")
+    k = torch.randn(1, 2, 300, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, 2, 300, device="cuda")
+    need = lib.fe_snap_workspace_floats(1, 4, 2, 300, 32)
+    ws = torch.empty(need, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    rc = lib.fe_snap_scores(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), out.data_ptr(),
+                            ws.data_ptr(), need - 1, 1, 4, 2, 300, 64, _lib.DTYPE_BF16, ctypes.c_float(0.125), 32, s)
+    assert rc == _lib.STATUS_INVALID and b"workspace" in lib.fe_last_error()
+    rc = lib.fe_snap_scores(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), out.data_ptr(),
+                            ws.data_ptr(), need, 1, 4, 2, 300, 64, _lib.DTYPE_BF16, ctypes.c_float(0.125), 32, s)
+    _lib.check(rc)
+    check_scores(out.cpu().numpy(), O.snap_scores(q.float().cpu().numpy(), k.float().cpu().numpy(), 32))

@@ -13,7 +13,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from common import GOLDEN, golden_cases, load_case
+from common import GOLDEN, golden_cases, load_case, snap_cases
 from oracle import restate as O
 
 
@@ -134,3 +134,19 @@ def test_flop_and_row_accounting():
     rows = O.scored_rows(8192, 0.1, 0)
     assert 860 < len(rows) < 890
     assert O.replay_flops(1, 28, 32768, 128, True, O.scored_rows(32768, 0.0, 128)) > 2.9e10
+
+
+def test_oracle_snap_matches_reference_fixtures():
+    # the reference's baselines.snap_scores / snap_select run here (torch, CPU)
+    for c in snap_cases():
+        s = O.snap_scores(c["q"].float().numpy(), c["k"].float().numpy(), c["window"], c["dtype_name"])
+        np.testing.assert_allclose(s, c["scores"], rtol=2e-5, atol=1e-7, err_msg=c["name"])
+        idx, keep = O.snap_select(c["scores"], c["budget"], c["window"])
+        np.testing.assert_array_equal(idx, c["idx"], err_msg=c["name"])
+        np.testing.assert_array_equal(keep, c["keep"], err_msg=c["name"])
+
+
+def test_round_to_dtype_matches_torch():
+    x = (torch.randn(10000, generator=torch.Generator().manual_seed(2)) * 300).float()
+    for name, dt in (("float16", torch.float16), ("bfloat16", torch.bfloat16)):
+        np.testing.assert_array_equal(O.round_to_dtype(x.numpy(), name), x.to(dt).float().numpy())
