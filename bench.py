@@ -362,6 +362,28 @@ def run_ours(args, w):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.profile in ("snap", "compact"):
+        # Short runs of the next rows for ncu: SnapKV scores, or the fused
+        # selection + K/V compaction on this workload's evict() importance.
+        from flash_evict.baselines import snap_scores
+        from flash_evict.compact import select_and_gather
+        imp = step(q, k, v)[1] if args.profile == "compact" else None
+
+        def one():
+            if args.profile == "snap":
+                snap_scores(q, k, 32)
+            else:
+                select_and_gather(imp, budget, k, v, reserved_recent=recent, pool_kernel=pool)
+
+        for _ in range(args.warmup + args.steps):
+            one()
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            print(json.dumps({"profile_run": args.workload, "target": args.profile, "steps": args.steps,
+                              "warmup": args.warmup, "device_status": _lib.device_status(local)}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     for _ in range(args.warmup):
         step(q, k, v)
     if args.profile:
@@ -535,7 +557,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", action="store_true", help="warm-up + K evict() steps only (for ncu)")
+    ap.add_argument("--profile", nargs="?", const="evict", choices=["evict", "snap", "compact"],
+                    help="warm-up + K calls only, for ncu: evict() steps (default), snap_scores(window=32), "
+                         "or select_and_gather on the workload's importance")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     w = WORKLOADS[args.workload]
