@@ -299,6 +299,27 @@ def next_rows(w, q, k, v, res, dev, stream):
         "snap_scores_tflops": snap_flops / (t_ss * 1e-3) / 1e12, "mass_per_row_check": s_sum / 32,
         "reference_published_a10g_ms": {"flash_snap_w32_32k_qwen_bf16": 130.904},
     }}
+    # Paired multi-policy selection (the reference's quality adapter selects
+    # once per method): 7 policies in one launch vs 7 back-to-back launches.
+    from flash_evict.policies import select_tokens_multi
+    vnorm = v.float().abs().sum(-1).contiguous()
+    pols = [(importance, 256, 0, 1), (importance, 256, 64, 1), (importance, 1024, 64, 1), (s_got, 256, 32, 5),
+            (s_got, 1024, 32, 5), (vnorm, 256, 0, 1), (importance, 256, 256, 1)]
+    pol_args = ([p_[0] for p_ in pols], [p_[1] for p_ in pols], [p_[2] for p_ in pols], [p_[3] for p_ in pols])
+
+    idx_sep = torch.empty((b, hkv, max(p_[1] for p_ in pols)), dtype=torch.int64, device=dev)
+
+    def separate():
+        for sc_, bud_, rec_, pool_ in pols:
+            _lib.check(lib.fe_select_tokens(sc_.data_ptr(), b * hkv, n, bud_, rec_, pool_, idx_sep.data_ptr(),
+                                            mask2.data_ptr(), 0, s))
+
+    t_multi = time_launch(lambda: select_tokens_multi(*pol_args), stream, dev)
+    t_sep = time_launch(separate, stream, dev)
+    extra["policies"] = {
+        "what": "paired-controller methods (fused r0/r64 at 256/1024, SnapKV 256/1024, value norm, uniform "
+                "recent): one fe_select_multi launch vs one fe_select_tokens launch per method",
+        "policies": len(pols), "one_launch_ms": t_multi, "separate_launches_ms": t_sep}
     return {**extra, "compaction": {
         "what": "KV compaction gather of the kept K/V rows (README.md:31 semantics), L2 flushed before each launch",
         "gather_ms": t_g, "select_ms": t_s, "select_gather_ms": t_sg,

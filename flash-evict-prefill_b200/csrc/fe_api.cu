@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -462,45 +463,62 @@ int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, con
 
 namespace {
 
-// Selection launch; with g != nullptr the same launch also compacts K/V.
-int select_impl(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
-                int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, const fe::GatherSpec* g,
-                void* stream) {
+// Selection launch for npol policies over the same rows x tokens shape; with
+// g[i] != nullptr policy i's launch also compacts K/V.
+int select_multi_impl(int64_t rows, int64_t tokens, int npol, const float* const* importance,
+                      const int64_t* budgets, const int64_t* recents, const int64_t* pools, int64_t* const* indices,
+                      uint8_t* const* masks, int mask_evict, const fe::GatherSpec* const* g, void* stream) {
   if (rows < 0 || tokens < 1) return fail(FE_STATUS_INVALID, "bad rows/tokens");
-  if (budget < 1 || budget > tokens) return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
-  if (recent < 0 || recent > budget) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
-  if (pool_kernel < 1 || pool_kernel % 2 != 1) return fail(FE_STATUS_INVALID, "pool_kernel must be a positive odd integer");
+  if (npol < 1 || npol > fe::SEL_MAX_POLICIES)
+    return fail(FE_STATUS_INVALID, "npolicies must be in [1, %d]", fe::SEL_MAX_POLICIES);
+  for (int i = 0; i < npol; ++i) {
+    if (budgets[i] < 1 || budgets[i] > tokens)
+      return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+    if (recents[i] < 0 || recents[i] > budgets[i]) return fail(FE_STATUS_INVALID, "recent must be an integer in [0, budget]");
+    if (pools[i] < 1 || pools[i] % 2 != 1) return fail(FE_STATUS_INVALID, "pool_kernel must be a positive odd integer");
+  }
   if (rows == 0) return FE_STATUS_OK;
-  if (!importance || !indices || !mask) return fail(FE_STATUS_INVALID, "null pointer");
-  int rc = bind_device(importance, nullptr);
+  for (int i = 0; i < npol; ++i)
+    if (!importance[i] || !indices[i] || !masks[i]) return fail(FE_STATUS_INVALID, "null pointer");
+  int rc = bind_device(importance[0], nullptr);
   if (rc) return rc;
-  const int64_t P = tokens - recent;
   const int64_t max_slice = 49152;  // keys per CTA held in shared memory (192 KiB)
-  // Cluster size: enough CTAs for the slice to fit in shared memory, and up
-  // to 8 for long rows (>= 4096 keys per CTA) so few rows still use many SMs.
+  // Cluster size (shared by the policies): enough CTAs for the longest past
+  // region to fit in shared memory, and up to 8 for long rows (>= 4096 keys
+  // per CTA) so few rows still use many SMs.
+  int64_t pmax = 0;
+  for (int i = 0; i < npol; ++i) pmax = std::max<int64_t>(pmax, tokens - recents[i]);
   int cl = 1;
-  while (cl < 16 && (P + cl - 1) / cl > max_slice) cl *= 2;
-  while (cl < 8 && P / (2 * cl) >= 4096) cl *= 2;
-  if ((P + cl - 1) / cl > max_slice)
+  while (cl < 16 && (pmax + cl - 1) / cl > max_slice) cl *= 2;
+  while (cl < 8 && pmax / (2 * cl) >= 4096) cl *= 2;
+  if ((pmax + cl - 1) / cl > max_slice)
     return fail(FE_STATUS_UNSUPPORTED, "sequence length %lld exceeds the selection limit (%lld)", (long long)tokens,
                 (long long)(max_slice * 16));
-  int64_t chunk = (P + cl - 1) / cl;
-  if (chunk < 1) chunk = 1;
-  if (rows * cl > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "too many rows");
-  fe::SelectParams p;
-  p.importance = importance;
-  p.N = tokens;
-  p.budget = budget;
-  p.recent = recent;
-  p.pool = (int)pool_kernel;
-  p.indices = indices;
-  p.mask = mask;
-  p.mask_evict = mask_evict ? 1 : 0;
-  p.chunk = chunk;
-  p.gather = g ? 1 : 0;
-  if (g) p.g = *g;
-  else memset(&p.g, 0, sizeof(p.g));
-  const int smem = (int)(chunk * 4);
+  if (rows * cl * npol > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "too many rows");
+  fe::SelectLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.rows = rows;
+  L.npol = npol;
+  int64_t max_chunk = 1;
+  for (int i = 0; i < npol; ++i) {
+    fe::SelectParams& p = L.pol[i];
+    const int64_t P = tokens - recents[i];
+    int64_t chunk = (P + cl - 1) / cl;
+    if (chunk < 1) chunk = 1;
+    max_chunk = std::max(max_chunk, chunk);
+    p.importance = importance[i];
+    p.N = tokens;
+    p.budget = budgets[i];
+    p.recent = recents[i];
+    p.pool = (int)pools[i];
+    p.indices = indices[i];
+    p.mask = masks[i];
+    p.mask_evict = mask_evict ? 1 : 0;
+    p.chunk = chunk;
+    p.gather = (g && g[i]) ? 1 : 0;
+    if (p.gather) p.g = *g[i];
+  }
+  const int smem = (int)(max_chunk * 4);
   rc = set_smem(fe::fe_select_kernel, smem < 49152 ? 49152 : smem);
   if (rc) return rc;
   if (cl > 8) {
@@ -509,7 +527,7 @@ int select_impl(const float* importance, int64_t rows, int64_t tokens, int64_t b
   }
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3((unsigned)(rows * cl));
+  cfg.gridDim = dim3((unsigned)(rows * cl * npol));
   cfg.blockDim = dim3(fe::SEL_THREADS);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
@@ -520,9 +538,18 @@ int select_impl(const float* importance, int64_t rows, int64_t tokens, int64_t b
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fe::fe_select_kernel, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fe::fe_select_kernel, L);
   if (e != cudaSuccess) return cuda_fail(e, "selection launch");
   return FE_STATUS_OK;
+}
+
+// Single-policy selection (with an optional gather).
+int select_impl(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
+                int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, const fe::GatherSpec* g,
+                void* stream) {
+  const fe::GatherSpec* gs[1] = {g};
+  return select_multi_impl(rows, tokens, 1, &importance, &budget, &recent, &pool_kernel, &indices, &mask, mask_evict,
+                           gs, stream);
 }
 
 }  // namespace
@@ -572,6 +599,34 @@ int fe_select_gather(const float* importance, int64_t batch, int64_t heads, int6
   if (rc) return rc;
   return select_impl(importance, batch * heads, tokens, budget, recent, pool_kernel, indices, mask, mask_evict, &g,
                      stream);
+}
+
+int fe_select_multi(const float* const* importance, int64_t batch, int64_t heads, int64_t tokens, int npolicies,
+                    const int64_t* budgets, const int64_t* recents, const int64_t* pool_kernels,
+                    int64_t* const* indices, uint8_t* const* masks, int mask_evict, const void* k,
+                    const int64_t* k_strides, const void* v, const int64_t* v_strides, void* const* k_outs,
+                    void* const* v_outs, int64_t channels, int64_t elem_bytes, void* stream) {
+  g_err[0] = 0;
+  if (batch < 0 || heads < 0 || tokens < 1) return fail(FE_STATUS_INVALID, "bad shape");
+  if (npolicies < 1 || npolicies > fe::SEL_MAX_POLICIES)
+    return fail(FE_STATUS_INVALID, "npolicies must be in [1, %d]", fe::SEL_MAX_POLICIES);
+  if (!importance || !budgets || !recents || !pool_kernels || !indices || !masks)
+    return fail(FE_STATUS_INVALID, "null pointer");
+  fe::GatherSpec specs[fe::SEL_MAX_POLICIES];
+  const fe::GatherSpec* gp[fe::SEL_MAX_POLICIES] = {nullptr};
+  if (k != nullptr) {
+    if (!k_outs) return fail(FE_STATUS_INVALID, "null pointer");
+    for (int i = 0; i < npolicies; ++i) {
+      if (budgets[i] < 1 || budgets[i] > tokens)
+        return fail(FE_STATUS_INVALID, "budget must be an integer in [1, sequence length]");
+      int rc = make_gather_spec(&specs[i], k, k_strides, v, v_strides, k_outs[i], v ? (v_outs ? v_outs[i] : nullptr) : nullptr,
+                                batch, heads, tokens, budgets[i], channels, elem_bytes);
+      if (rc) return rc;
+      gp[i] = &specs[i];
+    }
+  }
+  return select_multi_impl(batch * heads, tokens, npolicies, importance, budgets, recents, pool_kernels, indices, masks,
+                           mask_evict, gp, stream);
 }
 
 int fe_evict(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,

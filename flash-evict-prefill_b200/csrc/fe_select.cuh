@@ -51,6 +51,18 @@ struct SelectParams {
 constexpr int SEL_THREADS = 1024;
 constexpr int SEL_WARPS = SEL_THREADS / 32;
 
+// One launch selects for up to SEL_MAX_POLICIES policies (budget, reserved
+// suffix, pooling, score tensor, outputs) over the same rows x N shape, as the
+// paired multi-policy controller does for one prompt
+// (flash_evict/quality_adapter.py:95-111 choose_indices per method).  All
+// policies share the launch's cluster size; each has its own slice length.
+constexpr int SEL_MAX_POLICIES = 8;
+struct SelectLaunch {
+  int64_t rows;  // rows per policy
+  int npol;
+  SelectParams pol[SEL_MAX_POLICIES];
+};
+
 // Order-preserving map float -> uint32 (larger float -> larger key).
 __device__ __forceinline__ uint32_t order_key(float x) {
   if (x != x) return 0xFFFFFFFFu;  // NaN sorts above +inf
@@ -102,11 +114,14 @@ __device__ __forceinline__ void gather_share(const SelectParams& p, cg::cluster_
   gather_rows<2>(p.g, row, out_idx, a, e - a, threadIdx.x, SEL_THREADS);
 }
 
-__global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const SelectParams p) {
+__global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_constant__ SelectLaunch L) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
   const int crank = static_cast<int>(cluster.block_rank());
-  const int64_t row = blockIdx.x / C;
+  const int64_t cl_index = blockIdx.x / C;  // cluster index: (policy, row)
+  const int pi = static_cast<int>(cl_index / L.rows);
+  const int64_t row = cl_index - static_cast<int64_t>(pi) * L.rows;
+  const SelectParams& p = L.pol[pi];
 
   extern __shared__ uint32_t keys[];
   __shared__ uint32_t hist[2][256];

@@ -48,6 +48,8 @@ SIGNATURES = {
     "fe_gather_tokens": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _I64, _I64, _I64, _I64, _I64, _I64, _VP]),
     "fe_select_gather": (_INT, [_VP, _I64, _I64, _I64, _I64, _I64, _I64, _VP, _VP, _INT, _VP, _I64P, _VP, _I64P,
                                 _VP, _VP, _I64, _I64, _VP]),
+    "fe_select_multi": (_INT, [_VP, _I64, _I64, _I64, _INT, _VP, _VP, _VP, _VP, _VP, _INT, _VP, _I64P, _VP, _I64P,
+                               _VP, _VP, _I64, _I64, _VP]),
     "fe_evict_compact": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _I64,
                                 _I64, _I64, _I64, _INT, _INT, _F32, _F32, _I64, _INT, _I64, _I64, _I64, _VP]),
     "fe_snap_workspace_floats": (_I64, [_I64, _I64, _I64, _I64, _I64]),

@@ -134,6 +134,22 @@ FE_API int fe_select_gather(const float* importance, int64_t batch, int64_t head
                             int64_t recent, int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict,
                             const void* k, const int64_t* k_strides, const void* v, const int64_t* v_strides,
                             void* k_out, void* v_out, int64_t channels, int64_t elem_bytes, void* stream);
+/* Several selection policies in one launch: policy i selects budgets[i] tokens
+ * of importance[i] (contiguous FP32 [batch*heads, tokens]) with recents[i]
+ * reserved and pool_kernels[i] pooling, exactly as fe_select_tokens would,
+ * writing indices[i] ([batch*heads, budgets[i]]) and masks[i].  With k != NULL
+ * each policy also compacts K (and V, if not NULL) into k_outs[i] / v_outs[i]
+ * as fe_select_gather does.  Replaces the per-method selection loop of the
+ * paired multi-policy controller (flash_evict/quality_adapter.py:95-111,
+ * choose_indices at :39-51): methods sharing one prefill differ only in
+ * budget, reserved suffix and score tensor.  1 <= npolicies <= 8; the arrays
+ * (budgets, recents, pool_kernels, and the pointer arrays) are host memory. */
+FE_API int fe_select_multi(const float* const* importance, int64_t batch, int64_t heads, int64_t tokens,
+                           int npolicies, const int64_t* budgets, const int64_t* recents,
+                           const int64_t* pool_kernels, int64_t* const* indices, uint8_t* const* masks,
+                           int mask_evict, const void* k, const int64_t* k_strides, const void* v,
+                           const int64_t* v_strides, void* const* k_outs, void* const* v_outs, int64_t channels,
+                           int64_t elem_bytes, void* stream);
 /* fe_evict followed by the compaction of K and V into k_out/v_out
  * ([batch, kv_heads, budget, channels], dtype of the inputs), the selection
  * and the gather sharing one launch.  README.md:27-31 (evict, then gather). */

@@ -50,3 +50,23 @@ def test_evict_compact_keeps_the_evict_contract():
         evict_compact(q, q, q, 2, score=False)
     with pytest.raises(ValueError, match="CUDA"):
         evict_compact(q, q, q, 2)
+
+
+def test_multi_policy_argument_errors():
+    from flash_evict.policies import select_tokens_multi, select_and_gather_multi
+    s = torch.zeros(1, 2, 50)
+    with pytest.raises(ValueError, match="CUDA"):
+        select_tokens_multi(s, [10, 20])
+    with pytest.raises(ValueError, match="policies"):
+        select_tokens_multi(s, list(range(1, 10)))
+    with pytest.raises(ValueError, match="same shape"):
+        select_tokens_multi([s, torch.zeros(1, 2, 40)], [10, 20])
+    with pytest.raises(ValueError, match="one entry per policy"):
+        select_tokens_multi(s, [10, 20], recents=[1, 2, 3])
+    with pytest.raises(ValueError, match="budget"):
+        select_tokens_multi(s, [10, 60])
+    with pytest.raises(ValueError, match="recent"):
+        select_tokens_multi(s, [10, 20], recents=[11, 0])
+    k = torch.zeros(1, 2, 50, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        select_and_gather_multi(s, [10], k, k)
