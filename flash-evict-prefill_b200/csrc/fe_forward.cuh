@@ -70,6 +70,11 @@ struct FwdCfg {
 
 // Exponentials per 16 computed by exp2_poly instead of MUFU ex2.
 constexpr int FWD_POLY = 0;
+// Exponential pairs per 8 (16 exponentials) computed by exp2_poly_x2 (packed
+// FP32x2 on the FMA pipe) instead of MUFU ex2.  Measured at 2/3/4 pairs: the
+// attention kernel got 3 %/7 %/13 % slower (c3), so MUFU throughput is not
+// what bounds this softmax; kept at 0.
+constexpr int FWD_POLY_PAIRS = 0;
 // Softmax warpgroups take turns for their exponentials (see header).
 constexpr bool FWD_TURNS = false;
 
@@ -82,7 +87,7 @@ constexpr int FWD_REGS_NEEDED = (2 * 128 * FWD_REGS_HIGH + 128 * FWD_REGS_LOW + 
 // packed FP32x2 FMAs for the arguments, MUFU ex2 for the exponentials (POLY of
 // every 16 on the FMA pipe instead), packed adds into four pair accumulators,
 // and optionally the largest argument.  Returns the row sum; P is packed into pk.
-template <bool BF16, int POLY, bool TRACK_MAX>
+template <bool BF16, int POLY, bool TRACK_MAX, int POLYP = 0>
 __device__ __forceinline__ float softmax_exp_pass(const float (&x)[128], float sce, float m, uint32_t (&pk)[64],
                                                   float& amax) {
   const uint64_t sc2 = f2_pack(sce, sce);
@@ -96,12 +101,21 @@ __device__ __forceinline__ float softmax_exp_pass(const float (&x)[128], float s
   }
 #pragma unroll
   for (int c = 0; c < 128; c += 2) {
+    const uint64_t a2 = f2_fma(f2_pack(x[c], x[c + 1]), sc2, nm2);
     float a0, a1;
-    f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, nm2), a0, a1);
+    f2_unpack(a2, a0, a1);
     if (TRACK_MAX) am[(c >> 1) & 3] = fmax3(am[(c >> 1) & 3], a0, a1);
-    const float p0 = ((c & 15) >= 16 - POLY) ? exp2_poly(a0) : ex2_approx(a0);
-    const float p1 = (((c + 1) & 15) >= 16 - POLY) ? exp2_poly(a1) : ex2_approx(a1);
-    acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
+    float p0, p1;
+    uint64_t p2;
+    if (((c >> 1) & 7) < POLYP) {
+      p2 = exp2_poly_x2(a2);
+      f2_unpack(p2, p0, p1);
+    } else {
+      p0 = ((c & 15) >= 16 - POLY) ? exp2_poly(a0) : ex2_approx(a0);
+      p1 = (((c + 1) & 15) >= 16 - POLY) ? exp2_poly(a1) : ex2_approx(a1);
+      p2 = f2_pack(p0, p1);
+    }
+    acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], p2);
     pk[c >> 1] = pack2<BF16>(p0, p1);
   }
   amax = fmaxf(fmaxf(am[0], am[1]), fmaxf(am[2], am[3]));
@@ -421,7 +435,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       uint32_t pk[64];
       float amax;
-      const float tile_sum = softmax_exp_pass<BF16, FWD_POLY, false>(x, sce, m_used, pk, amax);
+      const float tile_sum = softmax_exp_pass<BF16, FWD_POLY, false, FWD_POLY_PAIRS>(x, sce, m_used, pk, amax);
       // Pass the turn to the other warpgroup if it has a tile to match.
       {
         const bool give = FWD_TURNS && ((t == 0) ? (j < n1) : (j + 1 < n0));
