@@ -19,8 +19,13 @@
 // relative error < 3e-6) and the exponent arithmetic uses packed FP32x2.  Query tiles whose
 // every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
 //
-// Roles (192 threads): warps 0-3 reduce (thread = key), warp 4 TMA producer,
-// warp 5 tcgen05 issuer and TMEM owner.  TMEM: two 128-column S^T buffers.
+// Roles (576 threads, one CTA per SM): warps 0-15 are four reduce warpgroups
+// (thread = key); warpgroup w takes items w, w+4, w+8, ... and owns TMEM
+// columns [128w, 128w+128) for their S^T, so four items are reduced at once
+// and every SM sub-partition has four warps to keep its MUFU busy.  Warp 16
+// is the TMA producer (K once, Q through a 4-deep ring), warp 17 the tcgen05
+// issuer and TMEM owner.  The four warpgroups' FP64 sums of a key are added in
+// a fixed order at the end (deterministic).
 #pragma once
 
 #include "fe_ptx.cuh"
@@ -48,19 +53,23 @@ constexpr int REPLAY_POLY = 2;
 
 template <int DP>
 struct ReplayCfg {
+  static constexpr int WGS = 4;                     // reduce warpgroups, one S^T buffer each
   static constexpr int TILE = 128 * DP * 2;
-  static constexpr int QST = 2;                     // Q tile ring depth
+  static constexpr int QST = 4;                     // Q tile ring depth
   static constexpr int NCH = DP / 64;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_Q = TILE;
-  static constexpr int OFF_BIAS = OFF_Q + QST * TILE;     // float[4 warps][2][128]
-  static constexpr int OFF_MAP = OFF_BIAS + 4 * 256 * 4;  // uint32 bitmap of listed query blocks
-  static constexpr int MAP_WORDS = 256;                   // up to 8192 blocks
+  static constexpr int OFF_BIAS = OFF_Q + QST * TILE;           // float[16 warps][2][128]
+  static constexpr int OFF_RED = OFF_BIAS + WGS * 4 * 256 * 4;  // double[WGS][128]
+  static constexpr int OFF_MAP = OFF_RED + WGS * 128 * 8;       // uint32 bitmap of listed query blocks
+  static constexpr int MAP_WORDS = 256;                         // up to 8192 blocks
   static constexpr int OFF_BAR = OFF_MAP + MAP_WORDS * 4;
-  // k_full, q_full[QST], q_empty[QST], s_full[2], s_free[2], drain
-  static constexpr int NBAR = 1 + 2 * QST + 5;
+  // k_full, q_full[QST], q_empty[QST], s_full[WGS], s_free[WGS], drain
+  static constexpr int NBAR = 1 + 2 * QST + 2 * WGS + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
-  static constexpr int THREADS = 192;
+  static constexpr int PRODUCER = WGS * 4;          // warp indices
+  static constexpr int ISSUER = WGS * 4 + 1;
+  static constexpr int THREADS = (WGS * 4 + 2) * 32;
 };
 
 // Iterates the CTA's (query tile, head-in-group) items in a fixed order.
@@ -81,6 +90,9 @@ struct ReplayItems {
     while (qt < qt_end && !listed(qt)) ++qt;
   }
   __device__ __forceinline__ bool valid() const { return qt < qt_end; }
+  __device__ __forceinline__ void advance(int n) {
+    for (int i = 0; i < n && valid(); ++i) next();
+  }
   __device__ __forceinline__ void next() {
     if (++g == G) {
       g = 0;
@@ -91,35 +103,49 @@ struct ReplayItems {
 };
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, 1)
     fe_replay_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const ReplayParams p) {
   using C = ReplayCfg<DP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* sbias = reinterpret_cast<float*>(smem + C::OFF_BIAS);
+  double* sred = reinterpret_cast<double*>(smem + C::OFF_RED);
   uint32_t* smap = reinterpret_cast<uint32_t*>(smem + C::OFF_MAP);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* k_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + C::QST;
   uint64_t* s_full = q_empty + C::QST;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* drain = s_free + 2;
+  uint64_t* s_free = s_full + C::WGS;
+  uint64_t* drain = s_free + C::WGS;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
 
-  // ---- work item: (key tile, b, hkv), key tiles of one (b, hkv) adjacent so
-  // the CTAs that stream the same Q rows run together and share them in L2 ----
+  // ---- work item: (key tile, b, hkv) ----
+  // Non-causal: every key tile has the same work; the key tiles of one
+  // (b, hkv) are adjacent so the CTAs that stream the same Q rows run together
+  // and share them in L2.  Causal: key tile kt has work proportional to the
+  // query tiles at or after it, so the key tiles are issued in ascending order
+  // across all (b, hkv) (heaviest first, longest-processing-time order).
   const int nqt = (p.N + 127) / 128;
-  int item = blockIdx.x;
-  const int kt = item % nqt;
-  item /= nqt;
-  const int hkv = item % p.Hkv;
-  const int b = item / p.Hkv;
+  int kt, hkv, b;
+  if (p.causal) {
+    const int nbh = p.B * p.Hkv;
+    kt = blockIdx.x / nbh;
+    const int bh = blockIdx.x - kt * nbh;
+    hkv = bh % p.Hkv;
+    b = bh / p.Hkv;
+  } else {
+    int item = blockIdx.x;
+    kt = item % nqt;
+    item /= nqt;
+    hkv = item % p.Hkv;
+    b = item / p.Hkv;
+  }
   const int qt_lo = max(p.s_lo / 128, p.causal ? kt : 0);
   const uint32_t* map = nullptr;
 
@@ -133,16 +159,16 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::WGS; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 4);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == C::ISSUER) {
     __syncwarp();
-    tmem_alloc(tmem_holder, 256);
+    tmem_alloc(tmem_holder, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -159,7 +185,7 @@ __global__ void __launch_bounds__(192, 2)
   const uint32_t tmem = *tmem_holder;
   const uint64_t TO = p.timeout_ns;
 
-  if (warp == 4) {
+  if (warp == C::PRODUCER) {
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       tma_prefetch_desc(&tq);
@@ -182,13 +208,13 @@ __global__ void __launch_bounds__(192, 2)
           for (int c = 0; c < C::NCH; ++c)
             tma_load_4d(smem + C::OFF_Q + s * C::TILE + c * 16384, &tq, &q_full[s], c * 64, it.qt * 128, hq, b);
         }
-        // Wait for the last load of each ring slot and for K before exiting.
+        // Every load must have landed before the CTA exits.
         mbar_wait_inflight(k_full, 0, TO);
         for (uint32_t i = (issued > C::QST ? issued - C::QST : 0); i < issued; ++i)
           mbar_wait_inflight(&q_full[i % C::QST], (i / C::QST) & 1, TO);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == C::ISSUER) {
     // ---------------------------------------------------------- MMA issuer --
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false);
@@ -201,10 +227,10 @@ __global__ void __launch_bounds__(192, 2)
         uint32_t i = 0;
         for (; it.valid() && ok; it.next(), ++i) {
           const int s = i % C::QST;
-          const int sb = i & 1;
+          const int sb = i % C::WGS;
           ok = mbar_wait(&q_full[s], (i / C::QST) & 1, TO, abort_flag);
           if (!ok) break;
-          if (i >= 2) ok = mbar_wait(&s_free[sb], ((i >> 1) - 1) & 1, TO, abort_flag);
+          if (i >= C::WGS) ok = mbar_wait(&s_free[sb], ((i / C::WGS) - 1) & 1, TO, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t qa = q_addr + s * C::TILE;
@@ -222,14 +248,17 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   } else {
-    // -------------------------------------------------------------- reduce --
-    const int kr = (warp << 5) + static_cast<int>(lane);  // key row in tile
+    // ------------------------------------------------ reduce (thread = key) --
+    const int wg = warp >> 2;                              // this warpgroup's items: wg, wg+4, ...
+    const int kr = ((warp & 3) << 5) + static_cast<int>(lane);  // key row in tile
     const int key = kt * 128 + kr;
-    const uint32_t lane_off = static_cast<uint32_t>(warp << 5) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) << 5) << 16;
+    const uint32_t tS = tmem + lane_off + wg * 128;
     const float sc = p.sc;
     double acc = 0.0;
     ReplayItems it;
     it.init(qt_lo, nqt, p.G, map);
+    it.advance(wg);
     // Row statistics {m, l} of an item's 128 query rows (4 per lane).
     auto load_stats = [&](const ReplayItems& x, float2* dst) {
       const float2* st =
@@ -254,53 +283,52 @@ __global__ void __launch_bounds__(192, 2)
         dst[c] = -bias;
       }
     };
-    // The bias of item i+1 is computed while item i is reduced (between its
-    // two 64-column halves); the statistics of item i+2 are prefetched then.
+    // The bias of this warpgroup's next item is computed while the current one
+    // is reduced; the statistics of the one after are prefetched then.
     float2 ml_next[4];
     if (it.valid()) {
       float2 ml0[4];
       load_stats(it, ml0);
       write_bias(it.qt, ml0, sbias + warp * 256);
       ReplayItems nx = it;
-      nx.next();
+      nx.advance(C::WGS);
       if (nx.valid()) load_stats(nx, ml_next);
     }
-    uint32_t i = 0;
+    uint32_t li = 0;  // this warpgroup's item count
     bool ok = true;
     const uint64_t sc2 = f2_pack(sc, sc);
-    for (; it.valid(); it.next(), ++i) {
-      const int sb = i & 1;
-      const float* wbias = sbias + warp * 256 + sb * 128;
+    for (; it.valid(); it.advance(C::WGS), ++li) {
+      const int bb = li & 1;
+      const float* wbias = sbias + warp * 256 + bb * 128;
       __syncwarp();  // this item's bias is written; the other buffer is free
-      ok = warp_all(mbar_wait(&s_full[sb], (i >> 1) & 1, TO, abort_flag));
+      ok = warp_all(mbar_wait(&s_full[wg], li & 1, TO, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const bool diag = p.causal && it.qt == kt;
       uint64_t acc2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
-      // exp2(x*sc - bias_q) summed over the 128 query columns, in two halves
-      // of 64 (fewer live registers, more exponentials in flight): packed
-      // FP32x2 FMA for the exponents, REPLAY_POLY of every 16 on the FMA pipe
-      // (exp2_poly) and the rest on MUFU, packed adds into four pair
-      // accumulators.  Diagonal tile: columns q < key are masked to -inf.
+      // exp2(x*sc - bias_q) over the 128 query columns in four 32-column
+      // quarters: packed FP32x2 FMA for the exponents, REPLAY_POLY of every 16
+      // on the FMA pipe (exp2_poly) and the rest on MUFU, packed adds into four
+      // pair accumulators.  Diagonal tile: columns q < key are masked to -inf.
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float x[64];
-        tmem_ld64_sync(tmem + lane_off + sb * 128 + h * 64, reinterpret_cast<uint32_t*>(x));
-        if (h == 1) {
+      for (int h = 0; h < 4; ++h) {
+        float x[32];
+        tmem_ld32_sync(tS + h * 32, reinterpret_cast<uint32_t*>(x));
+        if (h == 3) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[sb]);
+          if (lane == 0) mbar_arrive(&s_free[wg]);
         }
-        const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 64);
+        const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 32);
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
+        for (int c4 = 0; c4 < 8; ++c4) {
           const float4 nb = nb4[c4];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int c = c4 * 4 + hh * 2;
-            const int col = h * 64 + c;
+            const int col = h * 32 + c;
             float a0, a1;
             f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, hh == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w)),
                       a0, a1);
@@ -308,17 +336,17 @@ __global__ void __launch_bounds__(192, 2)
               a0 = (col >= kr) ? a0 : -INFINITY;
               a1 = (col + 1 >= kr) ? a1 : -INFINITY;
             }
-            const float p0 = ((c & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
-            const float p1 = (((c + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
+            const float p0 = ((col & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
+            const float p1 = (((col + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
             acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
           }
         }
-        if (h == 0) {
+        if (h == 1) {
           ReplayItems nx = it;
-          nx.next();
+          nx.advance(C::WGS);
           if (nx.valid()) {
-            write_bias(nx.qt, ml_next, sbias + warp * 256 + (sb ^ 1) * 128);
-            nx.next();
+            write_bias(nx.qt, ml_next, sbias + warp * 256 + (bb ^ 1) * 128);
+            nx.advance(C::WGS);
             if (nx.valid()) load_stats(nx, ml_next);
           }
         }
@@ -330,7 +358,11 @@ __global__ void __launch_bounds__(192, 2)
       f2_unpack(acc2[3], a6, a7);
       acc += static_cast<double>(((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7)));
     }
-    if (ok && key < p.N) {
+    // Combine the four warpgroups' sums of each key in a fixed order.
+    sred[wg * 128 + kr] = acc;
+    named_bar_sync(1, C::WGS * 128);
+    if (wg == 0 && !*abort_flag && key < p.N) {
+      const double total = ((sred[kr] + sred[128 + kr]) + sred[256 + kr]) + sred[384 + kr];
       float vn = 1.0f;
       if (p.weighted) {
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -344,16 +376,17 @@ __global__ void __launch_bounds__(192, 2)
         }
         vn = s;
       }
-      p.importance[(static_cast<size_t>(b) * p.Hkv + hkv) * p.N + key] = static_cast<float>(acc) * vn;
+      p.importance[(static_cast<size_t>(b) * p.Hkv + hkv) * p.N + key] = static_cast<float>(total) * vn;
     }
+    (void)ok;
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == C::ISSUER) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
