@@ -19,13 +19,14 @@
 // relative error < 3e-6) and the exponent arithmetic uses packed FP32x2.  Query tiles whose
 // every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
 //
-// Roles (576 threads, one CTA per SM): warps 0-15 are four reduce warpgroups
-// (thread = key); warpgroup w takes items w, w+4, w+8, ... and owns TMEM
-// columns [128w, 128w+128) for their S^T, so four items are reduced at once
-// and every SM sub-partition has four warps to keep its MUFU busy.  Warp 16
-// is the TMA producer (K once, Q through a 4-deep ring), warp 17 the tcgen05
-// issuer and TMEM owner.  The four warpgroups' FP64 sums of a key are added in
-// a fixed order at the end (deterministic).
+// Roles: REPLAY_WGS reduce warpgroups (thread = key) -- warpgroup w takes
+// items w, w+WGS, w+2*WGS, ... and owns TMEM columns [128w, 128w+128) for
+// their S^T, so WGS items are reduced at once -- then the TMA producer warp
+// (K once, Q through a WGS-deep ring) and the tcgen05 issuer / TMEM owner
+// warp.  4 warpgroups with one CTA per SM, or 2 with two CTAs per SM: either
+// way every SM sub-partition has four reduce warps to keep its MUFU busy.
+// The warpgroups' FP64 sums of a key are added in a fixed order at the end
+// (deterministic).
 #pragma once
 
 #include "fe_ptx.cuh"
@@ -50,12 +51,15 @@ struct ReplayParams {
 // Exponentials per 16 evaluated by exp2_poly (FMA pipe) instead of MUFU ex2;
 // the replay is MUFU-bound (16384 exponentials per 512-cycle S^T MMA).
 constexpr int REPLAY_POLY = 2;
+// Reduce warpgroups per CTA (2 or 4): 4 with one CTA per SM, or 2 with two.
+constexpr int REPLAY_WGS = 2;
 
 template <int DP>
 struct ReplayCfg {
-  static constexpr int WGS = 4;                     // reduce warpgroups, one S^T buffer each
+  static constexpr int WGS = REPLAY_WGS;            // reduce warpgroups, one S^T buffer each
+  static constexpr int CTAS_PER_SM = 4 / WGS;       // TMEM: WGS*128 columns per CTA
   static constexpr int TILE = 128 * DP * 2;
-  static constexpr int QST = 4;                     // Q tile ring depth
+  static constexpr int QST = WGS;                   // Q tile ring depth
   static constexpr int NCH = DP / 64;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_Q = TILE;
@@ -103,7 +107,7 @@ struct ReplayItems {
 };
 
 template <bool BF16, int DP>
-__global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, 1)
+__global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PER_SM)
     fe_replay_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const ReplayParams p) {
   using C = ReplayCfg<DP>;
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, 1)
   }
   if (warp == C::ISSUER) {
     __syncwarp();
-    tmem_alloc(tmem_holder, 512);
+    tmem_alloc(tmem_holder, C::WGS * 128);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -362,7 +366,9 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, 1)
     sred[wg * 128 + kr] = acc;
     named_bar_sync(1, C::WGS * 128);
     if (wg == 0 && !*abort_flag && key < p.N) {
-      const double total = ((sred[kr] + sred[128 + kr]) + sred[256 + kr]) + sred[384 + kr];
+      double total = sred[kr];
+#pragma unroll
+      for (int w = 1; w < C::WGS; ++w) total += sred[w * 128 + kr];
       float vn = 1.0f;
       if (p.weighted) {
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -386,7 +392,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, 1)
   if (warp == C::ISSUER) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, C::WGS * 128);
   }
 }
 
