@@ -473,46 +473,86 @@ def run_ours(args, w):
     attn_ms_max = max_over_ranks(attn_ms)
 
     # ---------------- end to end: host buffers, copies inside the region ---
-    # Host copies with the inputs' own strides (so each copy is one dense
-    # memcpy); a head-sharded rank copies only its own (batch, head) runs.
+    # Every step copies its inputs from pinned host memory (with the inputs'
+    # own strides, so each copy is one dense memcpy; a head-sharded rank copies
+    # only its own (batch, head) runs), runs evict() and reads the eviction
+    # decision (importance, indices, mask) back to pinned host memory; the
+    # attention output stays on the device for the next layer.  Copies run on
+    # their own streams, double-buffered: step i+1's inputs are copied in while
+    # step i computes.  The region runs from the first input copy to the last
+    # result read.
     def pinned_like(t):
         h_ = torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, pin_memory=True)
         h_.copy_(t)
         return h_
 
     hq_, hk_, hv_ = (pinned_like(t) for t in (q, k, v))
-    dq, dk, dv = (torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=dev) for t in (q, k, v))
-    if mode == "heads":
-        pieces = []
-        for b, h0, h1 in runs:
-            pieces += [(dq[b:b + 1, h0 * g:h1 * g], hq_[b:b + 1, h0 * g:h1 * g]),
-                       (dk[b:b + 1, h0:h1], hk_[b:b + 1, h0:h1]), (dv[b:b + 1, h0:h1], hv_[b:b + 1, h0:h1])]
-    else:
-        pieces = [(dq, hq_), (dk, hk_), (dv, hv_)]
-    h2d = sum(src.numel() * src.element_size() for _, src in pieces)
+    bufs = [tuple(torch.empty_strided(t.shape, t.stride(), dtype=t.dtype, device=dev) for t in (q, k, v))
+            for _ in range(2)]
+
+    def pieces_of(dq, dk, dv):
+        if mode == "heads":
+            out_ = []
+            for b, h0, h1 in runs:
+                out_ += [(dq[b:b + 1, h0 * g:h1 * g], hq_[b:b + 1, h0 * g:h1 * g]),
+                         (dk[b:b + 1, h0:h1], hk_[b:b + 1, h0:h1]), (dv[b:b + 1, h0:h1], hv_[b:b + 1, h0:h1])]
+            return out_
+        return [(dq, hq_), (dk, hk_), (dv, hv_)]
+
+    pieces = [pieces_of(*bf) for bf in bufs]
+    h2d = sum(src.numel() * src.element_size() for _, src in pieces[0])
+    h2d_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
     host_out = None
+    d2h = 0
+
+    def e2e_run(nsteps):
+        nonlocal host_out, d2h
+        loaded = [torch.cuda.Event() for _ in range(2)]
+        consumed = [None, None]
+        res_ = None
+
+        def load(i):
+            with torch.cuda.stream(h2d_stream):
+                if consumed[i % 2] is not None:
+                    h2d_stream.wait_event(consumed[i % 2])
+                for dst, src in pieces[i % 2]:
+                    dst.copy_(src, non_blocking=True)
+                loaded[i % 2].record(h2d_stream)
+
+        load(0)
+        for i in range(nsteps):
+            if i + 1 < nsteps:
+                load(i + 1)
+            stream.wait_event(loaded[i % 2])
+            res_ = step(*bufs[i % 2])
+            done = torch.cuda.Event()
+            done.record(stream)
+            consumed[i % 2] = done
+            decision = []
+            for r_ in (res_ if isinstance(res_, list) else [res_]):
+                decision.extend(t for t in r_[1:] if torch.is_tensor(t))
+            if host_out is None:
+                host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in decision]
+                d2h = sum(t.numel() * t.element_size() for t in decision)
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(done)
+                for h_, d_ in zip(host_out, decision):
+                    d_.record_stream(d2h_stream)
+                    h_.copy_(d_, non_blocking=True)
+        return res_
+
     e2e_steps = max(2, min(args.steps, 10))
+    e2e_run(2)  # warm-up of the pipelined loop
     barrier()
-    for it in range(e2e_steps + 1):
-        if it == 1:
-            barrier()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        for dst, src in pieces:
-            dst.copy_(src, non_blocking=True)
-        res = step(dq, dk, dv)
-        flat = []
-        for r_ in (res if isinstance(res, list) else [res]):
-            flat.extend(t for t in r_ if torch.is_tensor(t))
-        if host_out is None:
-            host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in flat]
-        for h_, d_ in zip(host_out, flat):
-            h_.copy_(d_, non_blocking=True)
-    e1.record(stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(h2d_stream)
+    res = e2e_run(e2e_steps)
+    e1.record(d2h_stream)
+    torch.cuda.synchronize(dev)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / e2e_steps
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
     e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
 
     extra = next_rows(w, q, k, v, res, dev, stream) if (world == 1 and mode == "replica") else None
@@ -554,7 +594,9 @@ def run_ours(args, w):
                      "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a multi-second loop)"},
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms},
+                "ms_per_step": e2e_ms,
+                "how": "per step: H2D of q/k/v from pinned host memory (double-buffered on a copy stream, "
+                       "overlapping the previous step's compute), evict(), D2H of importance/indices/mask"},
         "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }
