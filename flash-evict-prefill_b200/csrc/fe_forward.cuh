@@ -28,13 +28,12 @@
 // for exponentiation only moves when the true max exceeds it by more than
 // 2^8, which keeps P <= 256 and makes rescales rare.
 //
-// The two softmax warpgroups take turns for their exponentials (a token
-// passed through the turn[] mbarriers): while one warpgroup exponentiates,
-// the tensor pipe runs the other tile's PV and next S, and the two never
-// compete for the MUFU unit.  Without the token they fall into lock-step and
-// the tensor pipe idles half the time.  3 of every 16 exponentials run on the
-// FMA pipe (exp2_poly) so one warpgroup's turn is shorter than the other
-// tile's MMA work.
+// The softmax is written for the FP32x2 pipe (packed FMA for the exponent
+// arguments, packed adds for the row sums) with MUFU ex2 for the
+// exponentials.  Measured alternatives that were slower and are not used:
+// turn-taking between the two softmax warpgroups, a share of the
+// exponentials on the FMA pipe (FWD_POLY, FWD_POLY_PAIRS), scalar FP32
+// arithmetic, and double-buffered 64-key S tiles.
 #pragma once
 
 #include "fe_ptx.cuh"
@@ -61,9 +60,8 @@ struct FwdCfg {
   static constexpr int OFF_K = 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
   static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
-  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain,
-  // turn[2]
-  static constexpr int NBAR = 1 + 4 * STAGES + 9;
+  // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
+  static constexpr int NBAR = 1 + 4 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment slack
   static constexpr int THREADS = 384;
 };
@@ -75,8 +73,9 @@ constexpr int FWD_POLY = 0;
 // attention kernel got 3 %/7 %/13 % slower (c3), so MUFU throughput is not
 // what bounds this softmax; kept at 0.
 constexpr int FWD_POLY_PAIRS = 0;
-// Softmax warpgroups take turns for their exponentials (see header).
-constexpr bool FWD_TURNS = false;
+// Lazy rescale threshold (log2 units): the max used for the exponentials only
+// moves when the row's true max exceeds it by more than this, so P <= 2^this.
+constexpr float FWD_RESCALE_LOG2 = 8.0f;
 
 constexpr uint32_t FWD_REGS_HIGH = 216;
 constexpr uint32_t FWD_REGS_LOW = 64;
@@ -152,7 +151,6 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* drain = o_full + 2;
-  uint64_t* turn = drain + 1;  // turn[t]: warpgroup t may start its exponentials
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -210,8 +208,6 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&o_full[t], 1);
     }
     mbar_init(drain, 1);
-    mbar_init(&turn[0], 4);
-    mbar_init(&turn[1], 4);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -401,7 +397,7 @@ __global__ void __launch_bounds__(384, 1)
       const float m_new = fmaxf(m_used, row_max_scaled(x, sce));
       if (j == 0) {
         m_used = m_new;
-      } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
+      } else if (__any_sync(0xffffffffu, m_new > m_used + FWD_RESCALE_LOG2)) {
         // Rescale this warp's O rows; PV_t(j-1) is complete (see header).
         const float f = ex2_approx(m_used - m_new);
         l *= f;
@@ -416,32 +412,9 @@ __global__ void __launch_bounds__(384, 1)
         }
         tmem_wait_st();
       }
-      // Wait for this warpgroup's turn (the other one has finished the
-      // exponentials of its previous tile).
-      {
-        bool wait_turn;
-        uint32_t par;
-        if (t == 0) {
-          wait_turn = (j >= 1) && (j - 1 < n1);
-          par = (j - 1) & 1;
-        } else {
-          wait_turn = j < n0;
-          par = j & 1;
-        }
-        if (FWD_TURNS && wait_turn) {
-          ok = warp_all(mbar_wait(&turn[t], par, TO, abort_flag));
-          if (!ok) break;
-        }
-      }
       uint32_t pk[64];
       float amax;
       const float tile_sum = softmax_exp_pass<BF16, FWD_POLY, false, FWD_POLY_PAIRS>(x, sce, m_used, pk, amax);
-      // Pass the turn to the other warpgroup if it has a tile to match.
-      {
-        const bool give = FWD_TURNS && ((t == 0) ? (j < n1) : (j + 1 < n0));
-        __syncwarp();
-        if (give && lane == 0) mbar_arrive(&turn[t ^ 1]);
-      }
       l += tile_sum;
       tmem_st32(tS, pk);
       tmem_st32(tS + 32, pk + 32);
