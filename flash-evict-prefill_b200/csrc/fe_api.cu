@@ -70,7 +70,7 @@ int bind_device(const void* ptr, int* dev_out) {
   return FE_STATUS_OK;
 }
 
-int padded_dim(int64_t d) { return d <= 64 ? 64 : (d <= 128 ? 128 : 0); }
+int padded_dim(int64_t d) { return d <= 64 ? 64 : (d <= 128 ? 128 : (d <= 256 ? 256 : 0)); }
 
 // TMA map over a [B, H, N, D] view with element strides s[4] (s[3] == 1),
 // box = 64 channels x box_rows tokens, 128-byte swizzle, zero fill out of bounds.
@@ -115,7 +115,7 @@ int check_shapes(int64_t B, int64_t Hq, int64_t Hkv, int64_t N, int64_t D, int d
   if (Hq % Hkv) return fail(FE_STATUS_INVALID, "q_heads must be divisible by kv_heads");
   if (dtype != FE_DTYPE_F16 && dtype != FE_DTYPE_BF16) return fail(FE_STATUS_INVALID, "dtype must be f16 or bf16");
   if (D > 256) return fail(FE_STATUS_INVALID, "channels must be <= 256");
-  if (padded_dim(D) == 0) return fail(FE_STATUS_UNSUPPORTED, "channels > 128 are not supported by the sm_100a kernels");
+  if (padded_dim(D) == 0) return fail(FE_STATUS_UNSUPPORTED, "channels > 256 are not supported by the sm_100a kernels");
   if (N > (int64_t(1) << 30) || B * Hq > (int64_t(1) << 30)) return fail(FE_STATUS_UNSUPPORTED, "problem too large");
   return FE_STATUS_OK;
 }
@@ -145,17 +145,17 @@ int set_smem(K kernel, int bytes) {
   return FE_STATUS_OK;
 }
 
-template <bool BF16, int DP>
+template <bool BF16, int DQK, int DV>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const fe::FwdParams& p,
                int64_t items, cudaStream_t stream) {
-  using C = fe::FwdCfg<DP>;
-  auto kern = fe::fe_fwd_kernel<BF16, DP>;
+  using C = fe::FwdCfg<DQK, DV>;
+  auto kern = fe::fe_fwd_kernel<BF16, DQK, DV>;
   int rc = set_smem(kern, C::SMEM);
   if (rc) return rc;
   // The kernel moves registers between its warpgroups (setmaxnreg); that is
   // only safe if the launch allocation covers the split.  Refuse otherwise.
-  static int checked_regs[2][2] = {{0, 0}, {0, 0}};
-  int& regs = checked_regs[BF16 ? 1 : 0][DP == 64 ? 0 : 1];
+  static int checked_regs[2][3] = {{0, 0, 0}, {0, 0, 0}};
+  int& regs = checked_regs[BF16 ? 1 : 0][DQK == 64 ? 0 : (DQK == 128 ? 1 : 2)];
   if (regs == 0) {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
@@ -388,9 +388,22 @@ int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, con
   if (items > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int dp = padded_dim(channels);
+  p.vcol0 = 0;
+  if (dp == 256) {
+    // Two launches, one per 128-channel half of V and O; both compute the
+    // same S and row statistics (written by the first).
+    rc = dtype == FE_DTYPE_BF16 ? launch_fwd<true, 256, 128>(tq, tk, tv, p, items, s)
+                                : launch_fwd<false, 256, 128>(tq, tk, tv, p, items, s);
+    if (rc) return rc;
+    p.vcol0 = 128;
+    return dtype == FE_DTYPE_BF16 ? launch_fwd<true, 256, 128>(tq, tk, tv, p, items, s)
+                                  : launch_fwd<false, 256, 128>(tq, tk, tv, p, items, s);
+  }
   if (dtype == FE_DTYPE_BF16)
-    return dp == 64 ? launch_fwd<true, 64>(tq, tk, tv, p, items, s) : launch_fwd<true, 128>(tq, tk, tv, p, items, s);
-  return dp == 64 ? launch_fwd<false, 64>(tq, tk, tv, p, items, s) : launch_fwd<false, 128>(tq, tk, tv, p, items, s);
+    return dp == 64 ? launch_fwd<true, 64, 64>(tq, tk, tv, p, items, s)
+                    : launch_fwd<true, 128, 128>(tq, tk, tv, p, items, s);
+  return dp == 64 ? launch_fwd<false, 64, 64>(tq, tk, tv, p, items, s)
+                  : launch_fwd<false, 128, 128>(tq, tk, tv, p, items, s);
 }
 
 int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
@@ -455,8 +468,12 @@ int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, con
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int dp = padded_dim(channels);
   if (dtype == FE_DTYPE_BF16)
-    return dp == 64 ? launch_replay<true, 64>(tq, tk, p, items, s) : launch_replay<true, 128>(tq, tk, p, items, s);
-  return dp == 64 ? launch_replay<false, 64>(tq, tk, p, items, s) : launch_replay<false, 128>(tq, tk, p, items, s);
+    return dp == 64    ? launch_replay<true, 64>(tq, tk, p, items, s)
+           : dp == 128 ? launch_replay<true, 128>(tq, tk, p, items, s)
+                       : launch_replay<true, 256>(tq, tk, p, items, s);
+  return dp == 64    ? launch_replay<false, 64>(tq, tk, p, items, s)
+         : dp == 128 ? launch_replay<false, 128>(tq, tk, p, items, s)
+                     : launch_replay<false, 256>(tq, tk, p, items, s);
 }
 
 }  // extern "C"
@@ -716,10 +733,12 @@ int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k, const
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int dp = padded_dim(channels);
   if (dtype == FE_DTYPE_BF16)
-    return dp == 64 ? launch_snap<true, 64>(tq, tk, p, stats_items, score_items, s)
-                    : launch_snap<true, 128>(tq, tk, p, stats_items, score_items, s);
-  return dp == 64 ? launch_snap<false, 64>(tq, tk, p, stats_items, score_items, s)
-                  : launch_snap<false, 128>(tq, tk, p, stats_items, score_items, s);
+    return dp == 64    ? launch_snap<true, 64>(tq, tk, p, stats_items, score_items, s)
+           : dp == 128 ? launch_snap<true, 128>(tq, tk, p, stats_items, score_items, s)
+                       : launch_snap<true, 256>(tq, tk, p, stats_items, score_items, s);
+  return dp == 64    ? launch_snap<false, 64>(tq, tk, p, stats_items, score_items, s)
+         : dp == 128 ? launch_snap<false, 128>(tq, tk, p, stats_items, score_items, s)
+                     : launch_snap<false, 256>(tq, tk, p, stats_items, score_items, s);
 }
 
 int fe_device_status(int device, int clear, int* status_out) {

@@ -17,7 +17,7 @@
 // Registers: launched at 168/thread; the producer warpgroup drops to
 // FWD_REGS_LOW and the softmax warpgroups rise to FWD_REGS_HIGH
 // (2*128*216 + 128*64 = 63488 <= 384*168 = 64512).
-// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+DP), O1 after.
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+DV), O1 after.
 // P (16-bit) overwrites the first 64 columns of its S tile and feeds the PV
 // MMA straight from TMEM (A operand in TMEM, V as an MN-major B operand).
 //
@@ -48,18 +48,25 @@ struct FwdParams {
   int B, Hq, Hkv, N, D, G;
   float sc;           // scale * log2(e)
   int causal;
+  int vcol0;          // first V / output channel of this launch (0, or 128 for the second half of D > 128)
   uint64_t timeout_ns;
 };
 
-template <int DP>
+// DQK: channels of the QK^T contraction (64, 128 or 256, zero padded); DV:
+// channels of V (and O) this launch computes (64 or 128).  Heads with more
+// than 128 channels run two launches, one per 128-channel half of V, because
+// two 256-column O accumulators do not fit in TMEM next to the S tiles.
+template <int DQK, int DV>
 struct FwdCfg {
-  static constexpr int TILE = 128 * DP * 2;        // bytes of one 128-row tile
-  static constexpr int STAGES = (DP <= 64) ? 4 : 2;
-  static constexpr int NCH = DP / 64;              // 64-column swizzle chunks
+  static constexpr int TILE = 128 * DQK * 2;       // bytes of one 128-row Q or K tile
+  static constexpr int VTILE = 128 * DV * 2;       // bytes of one 128-row V tile
+  static constexpr int STAGES = (DQK <= 64) ? 4 : (DQK <= 128 ? 2 : 1);
+  static constexpr int NCH = DQK / 64;             // 64-column swizzle chunks of Q and K
+  static constexpr int NCHV = DV / 64;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = 2 * TILE;
   static constexpr int OFF_V = OFF_K + STAGES * TILE;
-  static constexpr int OFF_BAR = OFF_V + STAGES * TILE;
+  static constexpr int OFF_BAR = OFF_V + STAGES * VTILE;
   // barriers: q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], p_full[2], o_full[2], drain
   static constexpr int NBAR = 1 + 4 * STAGES + 7;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + tmem holder/abort + alignment slack
@@ -134,11 +141,11 @@ __device__ __forceinline__ float row_max_scaled(const float (&x)[128], float sce
   return fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7])) * sce;
 }
 
-template <bool BF16, int DP>
+template <bool BF16, int DQK, int DV>
 __global__ void __launch_bounds__(384, 1)
     fe_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const FwdParams p) {
-  using C = FwdCfg<DP>;
+  using C = FwdCfg<DQK, DV>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -250,9 +257,10 @@ __global__ void __launch_bounds__(384, 1)
           loads[s] = use * 2 + 1;  // K of this use in flight, V not issued
           break;
         }
-        mbar_expect_tx(&v_full[s], C::TILE);
-        for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(smem + C::OFF_V + s * C::TILE + c * 16384, &tv, &v_full[s], c * 64, j * 128, hkv, b);
+        mbar_expect_tx(&v_full[s], C::VTILE);
+        for (int c = 0; c < C::NCHV; ++c)
+          tma_load_4d(smem + C::OFF_V + s * C::VTILE + c * 16384, &tv, &v_full[s], p.vcol0 + c * 64, j * 128, hkv,
+                      b);
         loads[s] = use * 2 + 2;
       }
       // Never leave the CTA with a TMA write in flight: wait for the last load
@@ -269,7 +277,7 @@ __global__ void __launch_bounds__(384, 1)
     // ---------------------------------------------------------- MMA issuer --
     if (lane == 0 && nmax > 0) {
       constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false);
-      constexpr uint32_t ID_PV = idesc_f16(128, DP, BF16, true);
+      constexpr uint32_t ID_PV = idesc_f16(128, DV, BF16, true);
       const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
       const uint32_t k_addr = smem_u32(smem + C::OFF_K);
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
@@ -280,19 +288,20 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t dk = smem_desc_sw128(k_addr, 16, 1024);
       const uint64_t dv = smem_desc_sw128(v_addr, 16384, 1024);
       constexpr uint64_t TILE16 = C::TILE >> 4;
+      constexpr uint64_t VTILE16 = C::VTILE >> 4;
       auto issue_s = [&](int t, int s) {
         const uint64_t a = dq + t * TILE16;
         const uint64_t bb = dk + s * TILE16;
         const uint32_t d = tmem + t * 128;
-#pragma unroll
-        for (int kk = 0; kk < DP / 16; ++kk) {
+#pragma unroll 8
+        for (int kk = 0; kk < DQK / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
           umma_ss(d, a + off, bb + off, ID_S, kk > 0);
         }
       };
       auto issue_pv = [&](int t, int s, int j) {
-        const uint64_t bb = dv + s * TILE16;
-        const uint32_t d = tmem + 256 + t * DP;
+        const uint64_t bb = dv + s * VTILE16;
+        const uint32_t d = tmem + 256 + t * DV;
         const uint32_t pa = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -360,7 +369,7 @@ __global__ void __launch_bounds__(384, 1)
     const int row = rbase + r;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const uint32_t tS = tmem + lane_off + t * 128;
-    const uint32_t tO = tmem + lane_off + 256 + t * DP;
+    const uint32_t tO = tmem + lane_off + 256 + t * DV;
     const float sc = p.sc;
     // Positive scale: max on raw logits, scale folded into one FFMA per
     // element.  Otherwise scale first and use an effective scale of 1.
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(384, 1)
         l *= f;
         m_used = m_new;
 #pragma unroll 1
-        for (int c0 = 0; c0 < DP; c0 += 32) {
+        for (int c0 = 0; c0 < DV; c0 += 32) {
           uint32_t o[32];
           tmem_ld32_sync(tO + c0, o);
 #pragma unroll
@@ -428,19 +437,20 @@ __global__ void __launch_bounds__(384, 1)
       if (ok) {
         tc_fence_after();
         const bool live = row < p.N;
-        if (live) {
+        if (live && p.vcol0 == 0) {
           float2* st = reinterpret_cast<float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hq) * p.N + row;
           *st = make_float2(m_used, l);
         }
         const float inv = 1.0f / l;
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-        T* orow = reinterpret_cast<T*>(p.out) + ((static_cast<size_t>(b) * p.Hq + hq) * p.N + row) * p.D;
+        T* orow = reinterpret_cast<T*>(p.out) + ((static_cast<size_t>(b) * p.Hq + hq) * p.N + row) * p.D + p.vcol0;
+        const int dlim = p.D - p.vcol0;  // channels of this launch's half that exist
         const bool vec = (p.D % 8) == 0;
 #pragma unroll 1
-        for (int c0 = 0; c0 < DP; c0 += 32) {
+        for (int c0 = 0; c0 < DV; c0 += 32) {
           uint32_t o[32];
           tmem_ld32_sync(tO + c0, o);
-          if (live && c0 < p.D) {
+          if (live && c0 < dlim) {
             uint32_t w[16];
 #pragma unroll
             for (int c = 0; c < 16; ++c)
@@ -448,13 +458,13 @@ __global__ void __launch_bounds__(384, 1)
             if (vec) {
 #pragma unroll
               for (int q4 = 0; q4 < 4; ++q4) {
-                if (c0 + q4 * 8 < p.D)
+                if (c0 + q4 * 8 < dlim)
                   *reinterpret_cast<uint4*>(orow + c0 + q4 * 8) =
                       make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
               }
             } else {
               const uint16_t* h = reinterpret_cast<const uint16_t*>(w);
-              for (int c = 0; c < 32 && c0 + c < p.D; ++c) reinterpret_cast<uint16_t*>(orow)[c0 + c] = h[c];
+              for (int c = 0; c < 32 && c0 + c < dlim; ++c) reinterpret_cast<uint16_t*>(orow)[c0 + c] = h[c];
             }
           }
         }

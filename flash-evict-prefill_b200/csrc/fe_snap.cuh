@@ -82,7 +82,7 @@ struct SnapCfg {
   static constexpr int QHALF = 256 * 128;  // one 64-channel half of a 256-row group
   static constexpr int QBYTES = NCH * QHALF;
   static constexpr int KTILE = 128 * DP * 2;
-  static constexpr int KST = 3;  // K ring depth of the statistics pass
+  static constexpr int KST = DP <= 128 ? 3 : 1;  // K ring depth of the statistics pass (shared memory)
   static constexpr int THREADS = 192;
   // statistics pass: q_full, k_full[KST], k_empty[KST], s_full[2], s_free[2], drain
   static constexpr int A_OFF_Q = 0;

@@ -70,6 +70,7 @@ CASES = [  # (rows as (B, H), N, D, budget, recent, pool)
     ((1, 1), 500, 128, 500, 0, 1),       # budget == N
     ((1, 2), 200000, 128, 1024, 16, 1),  # large cluster
     ((4, 2), 3000, 80, 300, 7, 3),       # 160-byte rows
+    ((1, 2), 5000, 256, 500, 16, 5),     # 512-byte rows
 ]
 
 

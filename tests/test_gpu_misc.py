@@ -89,10 +89,18 @@ def test_watchdog_timeout_is_reported_not_hung():
     assert torch.isfinite(out.float()).all()
 
 
-def test_unsupported_head_dim_fails_loudly():
-    x = torch.randn(1, 1, 64, 192, device="cuda", dtype=torch.float16)
-    with pytest.raises(RuntimeError, match="unsupported"):
+def test_head_dim_above_256_is_rejected():
+    # the reference's contract (prefill.py:95-96): head dimension <= 256
+    x = torch.randn(1, 1, 64, 264, device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError, match="256"):
         prefill(x, x, x)
+    lib = _lib.load()
+    y = torch.empty_like(x)
+    st = torch.empty(1, 1, 64, 2, device="cuda")
+    rc = lib.fe_attention_fwd(x.data_ptr(), _lib.strides(x), x.data_ptr(), _lib.strides(x), x.data_ptr(),
+                              _lib.strides(x), y.data_ptr(), st.data_ptr(), 1, 1, 1, 64, 264, _lib.DTYPE_F16, 1,
+                              ctypes.c_float(0.06), None, 0, torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.STATUS_INVALID and b"256" in lib.fe_last_error()
 
 
 # --------------------------------------------------------- BASELINE configs --

@@ -64,6 +64,10 @@ def test_golden_reference_outputs(name):
     (137, 6, 2, 80, torch.float16, False),
     (65, 4, 1, 32, torch.bfloat16, True),
     (1, 2, 1, 16, torch.float16, True),
+    # more than 128 channels: two attention launches (one per 128-channel half of V)
+    (512, 4, 2, 256, torch.bfloat16, True),
+    (300, 4, 2, 192, torch.float16, True),
+    (257, 2, 1, 160, torch.bfloat16, False),
 ])
 def test_exact(n, h, hk, d, dtype, causal):
     # reference tests/test_prefill.py:15-41
