@@ -56,6 +56,11 @@ WORKLOADS = {
                     kw=dict(), sinks=False, qscale=1.0,
                     desc="reference benchmark shape B1 Hq28 Hkv4 N32768 D128 bf16 causal, all-query scoring, "
                          "budget 10%"),
+    # 256-channel heads (Gemma-style): not a BASELINE config; the attention
+    # runs as two launches, one per 128-channel half of V.
+    "d256": dict(b=1, hq=16, hkv=8, n=16384, d=256, dtype=torch.bfloat16, causal=True, budget=1638,
+                 kw=dict(recency_decay=0.1, reserved_recent=64), sinks=False, qscale=1.0,
+                 desc="B1 Hq16 Hkv8 N16384 D256 bf16 causal, decay 0.1, reserved 64, budget 10%"),
     "c5": dict(b=8, hq=32, hkv=32, n=4096, d=128, dtype=torch.float16, causal=False, budget=410,
                kw=dict(value_weighted=False), sinks=False, qscale=30.0, transposed=True, zero_v=0.05,
                desc="Batched MHA B8 Hq=Hkv=32 N4096 D128 fp16 noncausal, [B,N,H,D] strides, q x30, 5% zero V "
