@@ -14,6 +14,9 @@
  *    as the channel stride is 1, the other strides are multiples of 8 elements
  *    (16 bytes) and the base pointer is 16-byte aligned (the TMA rules).
  *  - dtype: FE_DTYPE_F16 or FE_DTYPE_BF16.  Q, K, V and the output share it.
+ *  - channels (head dimension): 1..256.  Up to 128 the attention is one
+ *    launch; 129..256 run as two launches on the stream, one per 128-channel
+ *    half of V and the output.
  *  - `stream` is a cudaStream_t passed as void*; every launch is asynchronous
  *    on it and no entry point synchronizes the host.
  *  - Return value: FE_STATUS_OK or an error code; fe_last_error() gives the
@@ -170,7 +173,7 @@ FE_API int fe_evict_compact(const void* q, const int64_t* q_strides, const void*
  * row statistics, then a key-stationary scoring pass); the w x tokens matrix
  * is never stored.  workspace: at least fe_snap_workspace_floats(...) floats,
  * 8-byte aligned, contents irrelevant.  Q/K layout rules as for
- * fe_attention_fwd; channels <= 128. */
+ * fe_attention_fwd; channels <= 256. */
 FE_API int64_t fe_snap_workspace_floats(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens,
                                         int64_t window);
 FE_API int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,

@@ -164,3 +164,28 @@ def test_no_oracle_on_product_path():
             if f.endswith((".py", ".cu", ".cuh")):
                 text = open(os.path.join(dirpath, f)).read()
                 assert "oracle" not in text.replace("oracle/", ""), f
+
+
+def _snap_workspace_model(b, hq, hk, n, window):
+    """Restates the SnapKV row-group and key-chunk geometry of the C ABI
+    (packed window rows in groups of <= 256, about one statistics CTA per SM,
+    at most 32 key chunks) to check fe_snap_workspace_floats on the host."""
+    g = hq // hk
+    w = min(window, n)
+    w8 = (w + 7) // 8 * 8
+    groups = -(-g // (256 // w8)) if w8 <= 256 else g * (-(-w // 256))
+    units = b * hk * groups
+    ntiles = -(-n // 128)
+    nchunk = max(1, min(-(-148 // units), 32, ntiles))
+    tiles = -(-ntiles // nchunk)
+    nchunk = -(-ntiles // tiles)
+    return units * nchunk * 256 * 2
+
+
+@pytest.mark.parametrize("shape", [(1, 28, 4, 32768, 32), (1, 6, 2, 137, 137), (2, 8, 2, 200, 48),
+                                   (1, 2, 1, 600, 300), (8, 32, 32, 4096, 32), (1, 4, 1, 1, 32)])
+def test_snap_workspace_size_on_host(shape):
+    lib = _lib.load()
+    assert lib.fe_snap_workspace_floats(*shape) == _snap_workspace_model(*shape)
+    assert lib.fe_snap_workspace_floats(1, 28, 4, 32768, 0) < 0
+    assert lib.fe_snap_workspace_floats(1, 27, 4, 32768, 32) < 0  # q_heads not a multiple of kv_heads
