@@ -1,0 +1,72 @@
+"""Seeded random configurations of the whole path against the oracle.
+
+Each case draws a shape (batch, query/KV heads, tokens, channels 16..256),
+dtype, causality, layout ([B,H,N,D] or the adapters' [B,N,H,D] view),
+logit scale and scoring options, then checks evict() against the numpy
+restatement with the reference's tolerances (tests/test_prefill.py:15-41),
+the compacted K/V bitwise against torch.gather, and SnapKV scores against
+the restated baseline.  Sizes stay small so the oracle runs in seconds.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from common import selection_mismatch
+from flash_evict import evict_compact
+from flash_evict.baselines import snap_scores
+from oracle import restate as O
+
+pytestmark = pytest.mark.gpu
+
+
+def draw(seed):
+    r = np.random.default_rng(seed)
+    hk = int(r.choice([1, 2, 4]))
+    g = int(r.choice([1, 2, 3, 7]))
+    d = int(r.choice([16, 32, 64, 80, 96, 128, 160, 192, 256]))
+    return dict(b=int(r.choice([1, 2])), hk=hk, h=hk * g, n=int(r.integers(1, 700)), d=d,
+                dtype=torch.bfloat16 if r.random() < 0.5 else torch.float16, causal=bool(r.random() < 0.7),
+                transposed=bool(r.random() < 0.5), qscale=float(r.choice([0.25, 1.0, 4.0])),
+                decay=float(r.choice([0.0, 0.0, 0.05])), window=int(r.choice([0, 0, 32, 100])),
+                weighted=bool(r.random() < 0.7), pool=int(r.choice([1, 1, 5])), frac=float(r.choice([0.1, 0.3])),
+                snap_window=int(r.choice([1, 8, 32, 77])))
+
+
+@pytest.mark.parametrize("seed", range(48))
+def test_random_configuration(seed):
+    c = draw(seed)
+    g = torch.Generator().manual_seed(seed)
+    b, h, hk, n, d = c["b"], c["h"], c["hk"], c["n"], c["d"]
+    if c["transposed"]:
+        mk = lambda heads: torch.randn(b, n, heads, d, generator=g).to(c["dtype"]).cuda().transpose(1, 2)
+    else:
+        mk = lambda heads: torch.randn(b, heads, n, d, generator=g).to(c["dtype"]).cuda()
+    q = (mk(h).float() * c["qscale"]).to(c["dtype"])
+    k, v = mk(hk), mk(hk)
+    budget = max(1, math.ceil(n * c["frac"]))
+    recent = min(budget, 8) if seed % 3 == 0 else 0
+    kw = dict(causal=c["causal"], recency_decay=c["decay"], observation_window=c["window"],
+              value_weighted=c["weighted"])
+    out, imp, idx, mask, k_kept, v_kept = evict_compact(q, k, v, budget, reserved_recent=recent,
+                                                        pool_kernel=c["pool"], **kw)
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    ref_out, ref_imp = O.materialized(qn, kn, vn, causal=c["causal"], recency_decay=c["decay"],
+                                      observation_window=c["window"], value_weighted=c["weighted"])
+    tol = 0.012 if c["dtype"] == torch.bfloat16 else 0.002
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref_out, atol=tol * max(1.0, c["qscale"]), rtol=0.006,
+                               err_msg=str(c))
+    np.testing.assert_allclose(imp.cpu().numpy(), ref_imp, atol=3e-3, rtol=3e-4, err_msg=str(c))
+    _, ref_keep = O.select_tokens(ref_imp, budget, reserved_recent=recent, pool_kernel=c["pool"])
+    mism, ok = selection_mismatch(~mask.cpu().numpy(), ref_keep, imp.cpu().numpy(), ref_imp, 3e-3, 3e-4)
+    assert ok, (c, mism)
+    assert (~mask).sum(-1).eq(budget).all()
+    gather = lambda x: x.gather(2, idx[..., None].expand(-1, -1, -1, d))
+    assert torch.equal(k_kept, gather(k)) and torch.equal(v_kept, gather(v))
+    if c["dtype"] == torch.bfloat16 or c["qscale"] <= 1.0:
+        s = snap_scores(q, k, c["snap_window"]).cpu().numpy()
+        ref_s = O.snap_scores(qn, kn, c["snap_window"], str(c["dtype"]).split(".")[-1])
+        rel = np.abs(s - ref_s) / (np.abs(ref_s) + 1e-6)
+        assert np.quantile(rel, 0.99) < 1e-4 and rel.max() < 2e-2, (c, float(rel.max()))
+        np.testing.assert_allclose(s.sum(-1), min(c["snap_window"], n), rtol=1e-4)
