@@ -211,8 +211,11 @@ def run_reference(args, w):
     q, k, v = make_inputs(w, 0, "cpu")
     vals = []
     desc, threads = "", 1
+    # Each step is a bounded sample sized so the whole --steps/--warmup run
+    # stays within about two minutes of CPU time (one 256-row chunk at least).
+    per_step = min(8.0, max(0.2, 120.0 / max(1, args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
-        val, desc, threads = cpu_oracle_sample(w, q, k, v, seconds=4.0 if i < args.warmup else 8.0)
+        val, desc, threads = cpu_oracle_sample(w, q, k, v, seconds=per_step)
         if i >= args.warmup:
             vals.append(val)
     value = statistics.median(vals)
