@@ -411,7 +411,23 @@ int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, con
                      int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype, int causal,
                      float scale, float recency_decay, int64_t observation_window, int value_weighted,
                      const int32_t* query_blocks, int64_t num_query_blocks, void* stream) {
+  return fe_replay_scores_range(q, q_strides, k, k_strides, v, v_strides, row_stats, importance, batch, q_heads,
+                                kv_heads, tokens, channels, dtype, causal, scale, recency_decay, observation_window,
+                                value_weighted, query_blocks, num_query_blocks, 0, (tokens + 127) / 128, stream);
+}
+
+int fe_replay_scores_range(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                           const void* v, const int64_t* v_strides, const float* row_stats, float* importance,
+                           int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels,
+                           int dtype, int causal, float scale, float recency_decay, int64_t observation_window,
+                           int value_weighted, const int32_t* query_blocks, int64_t num_query_blocks,
+                           int64_t key_tile_begin, int64_t key_tile_end, void* stream) {
   g_err[0] = 0;
+  const int64_t ntiles_all = (tokens + 127) / 128;
+  if (key_tile_begin < 0 || key_tile_end > ntiles_all || key_tile_begin > key_tile_end)
+    return fail(FE_STATUS_INVALID, "key tile range [%lld, %lld) outside [0, %lld)", (long long)key_tile_begin,
+                (long long)key_tile_end, (long long)ntiles_all);
+  if (key_tile_begin == key_tile_end) return FE_STATUS_OK;
   int rc = check_shapes(batch, q_heads, kv_heads, tokens, channels, dtype);
   if (rc) return rc;
   if (!q || !k || !v || !row_stats || !importance) return fail(FE_STATUS_INVALID, "null pointer");
@@ -463,7 +479,9 @@ int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, con
   p.causal = causal ? 1 : 0;
   p.weighted = value_weighted ? 1 : 0;
   p.timeout_ns = (uint64_t)g_watchdog_ns;
-  const int64_t items = ((tokens + 127) / 128) * batch * kv_heads;
+  p.kt0 = (int)key_tile_begin;
+  p.nkt = (int)(key_tile_end - key_tile_begin);
+  const int64_t items = (int64_t)p.nkt * batch * kv_heads;
   if (items > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int dp = padded_dim(channels);

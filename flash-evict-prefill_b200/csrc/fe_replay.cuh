@@ -45,6 +45,7 @@ struct ReplayParams {
   float decay_log2;         // recency_decay * log2(e)
   int s_lo;                 // first scored row (window and underflow cut)
   int causal, weighted;
+  int kt0, nkt;             // key tiles [kt0, kt0 + nkt) of this launch
   uint64_t timeout_ns;
 };
 
@@ -145,11 +146,12 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     b = bh / p.Hkv;
   } else {
     int item = blockIdx.x;
-    kt = item % nqt;
-    item /= nqt;
+    kt = item % p.nkt;
+    item /= p.nkt;
     hkv = item % p.Hkv;
     b = item / p.Hkv;
   }
+  kt += p.kt0;
   const int qt_lo = max(p.s_lo / 128, p.causal ? kt : 0);
   const uint32_t* map = nullptr;
 

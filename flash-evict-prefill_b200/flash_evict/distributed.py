@@ -8,16 +8,23 @@ head  -- the (batch, kv-head) units are independent: every rank takes a
          whole evict() path locally.  No communication.
 query -- for long contexts: query rows are dealt out in 256-row blocks
          (FE_QUERY_BLOCK) in a causal-balanced snake order.  Every rank holds
-         the full K/V, computes the attention output of its own rows and the
-         partial importance contributed by its rows, then one
-         all_reduce(SUM) of the FP32 [B, Hkv, N] scores gives every rank the
-         full importance, and each rank runs the (identical) selection.
-         The attention output can optionally be all-gathered.
+         the full K/V and computes the attention output and softmax row
+         statistics of its own rows.  The scored rows (the observation
+         window, or the rows a recency decay leaves above FP32 underflow)
+         usually sit in a few blocks at the end, so the replay is balanced
+         separately: the statistics of the scored rows are exchanged (one
+         small all_reduce), every rank replays all scored rows against its
+         own contiguous range of key tiles, and one all_reduce(SUM) of the
+         FP32 [B, Hkv, N] scores (each key written by exactly one rank,
+         zeros elsewhere) gives every rank the full importance; each rank
+         then runs the (identical) selection.  The attention output can
+         optionally be all-gathered.
 
-The all-reduce makes the summation order of the importance depend on the
-collective's algorithm, so it is reproducible for a fixed world size and
-NCCL configuration but not bitwise equal across world sizes.
+Each importance value is computed by one rank with the same kernel, inputs
+and summation order as on a single GPU, so the result is bitwise equal to
+single-GPU evict() for any world size.
 """
+import math
 import torch
 import torch.distributed as dist
 
@@ -25,7 +32,8 @@ from . import _lib
 from .prefill import (_attention, _check_prefill_args, _check_select_args, _replay, _select, _tma_view,
                       _validate)
 
-__all__ = ["query_block_plan", "head_unit_plan", "evict_query_sharded", "evict_head_sharded"]
+__all__ = ["query_block_plan", "head_unit_plan", "key_tile_plan", "first_scored_row", "evict_query_sharded",
+           "evict_head_sharded"]
 
 BLOCK = _lib.QUERY_BLOCK
 
@@ -57,6 +65,26 @@ def query_block_plan(n_tokens, world, causal=True):
         rank = pos if rnd % 2 == 0 else world - 1 - pos
         plan[rank].append(blk)
     return plan
+
+
+def key_tile_plan(n_tokens, world):
+    """Split the ceil(n_tokens/128) key tiles into `world` contiguous ranges
+    (begin, end), one per rank."""
+    nkt = (n_tokens + 127) // 128
+    return [(nkt * r // world, nkt * (r + 1) // world) for r in range(world)]
+
+
+def first_scored_row(n_tokens, recency_decay=0.0, observation_window=0):
+    """First query row that carries weight in the replay: the start of the
+    observation window, raised past rows whose FP32 weight
+    exp(-decay * distance) is below 2^-127 (the rows the replay kernel skips)."""
+    w = n_tokens if observation_window == 0 or observation_window > n_tokens else observation_window
+    lo = n_tokens - w
+    if recency_decay > 0:
+        reach = 127.0 / (recency_decay * math.log2(math.e))
+        if reach < n_tokens:
+            lo = max(lo, n_tokens - 1 - int(math.floor(reach)))
+    return lo
 
 
 def head_unit_plan(batch, kv_heads, world):
@@ -103,26 +131,41 @@ def evict_head_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recent
     return results
 
 
-def _cuda_partial(q, k, v, blocks, causal, scale, recency_decay, observation_window, value_weighted, marks=None):
-    """This rank's attention rows and partial importance, on its GPU."""
+def _cuda_attend(q, k, v, blocks, causal, scale):
+    """This rank's attention rows and their softmax row statistics."""
     b, h, n, d = q.shape
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     row_stats = torch.empty((b, h, n, 2), dtype=torch.float32, device=q.device)
-    importance = torch.empty((b, k.shape[1], n), dtype=torch.float32, device=q.device)
-    blk = torch.tensor(blocks, dtype=torch.int32, device=q.device)
-    qv, kv, vv = _tma_view(q), _tma_view(k), _tma_view(v)
+    if len(blocks):
+        blk = torch.tensor(blocks, dtype=torch.int32, device=q.device)
+        with torch.cuda.device(q.device):
+            _attention(_tma_view(q), _tma_view(k), _tma_view(v), out, row_stats, causal, scale, query_blocks=blk)
+    return out, row_stats
+
+
+def _cuda_replay(q, k, v, row_stats, key_tiles, causal, scale, recency_decay, observation_window, value_weighted):
+    """Importance of this rank's key tiles from every scored row; zeros for
+    the other keys."""
+    importance = torch.zeros((q.shape[0], k.shape[1], q.shape[2]), dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
-        if marks:
-            marks("start")
-        if len(blocks):
-            _attention(qv, kv, vv, out, row_stats, causal, scale, query_blocks=blk)
-        if marks:
-            marks("attention")
-        _replay(qv, kv, vv, row_stats, importance, causal, scale, recency_decay, observation_window,
-                value_weighted, query_blocks=blk)
-        if marks:
-            marks("replay")
-    return out, importance
+        _replay(_tma_view(q), _tma_view(k), _tma_view(v), row_stats, importance, causal, scale, recency_decay,
+                observation_window, value_weighted, key_tiles=key_tiles)
+    return importance
+
+
+def _exchange_stats(row_stats, blocks, r0, group):
+    """Give every rank the statistics of all scored rows [r0, n): each rank
+    contributes the rows of its own blocks, zeros elsewhere, all_reduce(SUM)."""
+    n = row_stats.shape[2]
+    if r0 >= n:
+        return
+    part = torch.zeros_like(row_stats[:, :, r0:])
+    for blk in blocks:
+        lo, hi = max(r0, blk * BLOCK), min(n, (blk + 1) * BLOCK)
+        if lo < hi:
+            part[:, :, lo - r0:hi - r0] = row_stats[:, :, lo:hi]
+    dist.all_reduce(part, op=dist.ReduceOp.SUM, group=group)
+    row_stats[:, :, r0:] = part
 
 
 def _gather_rows(out, plan, rank, group):
@@ -146,15 +189,23 @@ def _gather_rows(out, plan, rank, group):
 
 
 def _query_sharded(q, k, v, budget, recent, pool_kernel, causal, scale, recency_decay, observation_window,
-                   value_weighted, gather_output, group, partial_fn, select_fn, marks=None):
+                   value_weighted, gather_output, group, attend_fn, replay_fn, select_fn, marks=None):
     rank, world = _world(group)
-    plan = query_block_plan(q.shape[2], world, causal)
+    n = q.shape[2]
+    plan = query_block_plan(n, world, causal)
     if marks:
-        out, importance = partial_fn(q, k, v, plan[rank], causal, scale, recency_decay, observation_window,
-                                     value_weighted, marks=marks)
-    else:
-        out, importance = partial_fn(q, k, v, plan[rank], causal, scale, recency_decay, observation_window,
-                                     value_weighted)
+        marks("start")
+    out, row_stats = attend_fn(q, k, v, plan[rank], causal, scale)
+    if marks:
+        marks("attention")
+    if world > 1:
+        _exchange_stats(row_stats, plan[rank], first_scored_row(n, recency_decay, observation_window), group)
+        if marks:
+            marks("stats")
+    importance = replay_fn(q, k, v, row_stats, key_tile_plan(n, world)[rank], causal, scale, recency_decay,
+                           observation_window, value_weighted)
+    if marks:
+        marks("replay")
     if world > 1:
         dist.all_reduce(importance, op=dist.ReduceOp.SUM, group=group)
     if marks:
@@ -186,4 +237,4 @@ def evict_query_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recen
         return _select(importance, budget_, recent_, pool_, evict_mask=True)
 
     return _query_sharded(q, k, v, budget, recent, pool_kernel, causal, scale, recency_decay, observation_window,
-                          value_weighted, gather_output, group, _cuda_partial, select_fn, marks=_marks)
+                          value_weighted, gather_output, group, _cuda_attend, _cuda_replay, select_fn, marks=_marks)

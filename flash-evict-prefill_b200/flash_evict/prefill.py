@@ -123,15 +123,18 @@ def _attention(q, k, v, out, row_stats, causal, scale, query_blocks=None):
 
 
 def _replay(q, k, v, row_stats, importance, causal, scale, recency_decay, observation_window, value_weighted,
-            query_blocks=None):
+            query_blocks=None, key_tiles=None):
+    """Importance replay; key_tiles=(begin, end) restricts it to those
+    128-key tiles (the rest of `importance` is left untouched)."""
     lib = _lib.load()
     b, h, n, d = q.shape
     qb, nqb = _blocks_arg(query_blocks)
-    _lib.check(lib.fe_replay_scores(
+    kt0, kt1 = key_tiles if key_tiles is not None else (0, (n + 127) // 128)
+    _lib.check(lib.fe_replay_scores_range(
         q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
         row_stats.data_ptr(), importance.data_ptr(), b, h, k.shape[1], n, d, _dtype_code(q.dtype),
         1 if causal else 0, float(scale), float(recency_decay), int(observation_window),
-        1 if value_weighted else 0, qb, nqb, _stream(q.device)))
+        1 if value_weighted else 0, qb, nqb, int(kt0), int(kt1), _stream(q.device)))
 
 
 def _select(importance, budget, recent, pool_kernel, evict_mask):

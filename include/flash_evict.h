@@ -88,6 +88,21 @@ FE_API int fe_replay_scores(const void* q, const int64_t* q_strides, const void*
                      int dtype, int causal, float scale, float recency_decay, int64_t observation_window,
                      int value_weighted, const int32_t* query_blocks, int64_t num_query_blocks, void* stream);
 
+/* fe_replay_scores restricted to the key tiles [key_tile_begin, key_tile_end)
+ * (128 keys each): only importance[b, hkv, 128*key_tile_begin ..
+ * 128*key_tile_end) is written, summed over all scored query rows (or the
+ * listed query blocks).  A query-sharded job uses it to split the replay
+ * evenly by keys across ranks when the scored rows are concentrated in a few
+ * query blocks (recency decay, observation window): each rank needs the row
+ * statistics of every scored row, and the ranks' key ranges are then
+ * combined.  No counterpart in the reference (single GPU). */
+FE_API int fe_replay_scores_range(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                                  const void* v, const int64_t* v_strides, const float* row_stats,
+                                  float* importance, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                  int64_t tokens, int64_t channels, int dtype, int causal, float scale,
+                                  float recency_decay, int64_t observation_window, int value_weighted,
+                                  const int32_t* query_blocks, int64_t num_query_blocks, int64_t key_tile_begin,
+                                  int64_t key_tile_end, void* stream);
 /* Token selection.  Replaces `select_tokens` (flash_evict/prefill.py:140-170).
  * importance: contiguous FP32 [rows, tokens].  For each row: the past region
  * is the first tokens-recent scores; if pool_kernel > 1 and budget > recent it

@@ -17,7 +17,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from flash_evict.distributed import _query_sharded, head_unit_plan, query_block_plan, _block_cost, BLOCK
+from flash_evict.distributed import (BLOCK, _block_cost, _query_sharded, first_scored_row, head_unit_plan,
+                                     key_tile_plan, query_block_plan)
 from oracle import restate as O
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -55,16 +56,49 @@ def test_head_unit_plan_covers_units(batch, heads, world):
     assert max(sizes) - min(sizes) <= 1
 
 
-def _oracle_partial(q, k, v, blocks, causal, scale, decay, window, weighted):
-    n = q.shape[2]
-    rows = np.concatenate([np.arange(b * BLOCK, min(n, (b + 1) * BLOCK)) for b in blocks]) if blocks else \
-        np.zeros(0, dtype=np.int64)
-    out, mass = O.chunked(q, k, v, causal=causal, value_weighted=weighted, scale=scale, recency_decay=decay,
-                          observation_window=window, out_rows=rows, score_rows=rows)
-    if out is None:
-        out = np.zeros(q.shape, dtype=np.float32)
-    out = np.nan_to_num(out, nan=0.0)
-    return torch.from_numpy(out), torch.from_numpy(mass)
+def _oracle_attend(q, k, v, blocks, causal, scale):
+    """Attention rows of the given query blocks and their softmax statistics
+    {m (log2 units), l}, computed in numpy (float64); other rows zero."""
+    qn, kn, vn = (t.double().numpy() for t in (q, k, v))
+    b, h, n, d = qn.shape
+    g = h // kn.shape[1]
+    out = np.zeros(qn.shape)
+    stats = np.zeros((b, h, n, 2))
+    rows = [r for blk in blocks for r in range(blk * BLOCK, min(n, (blk + 1) * BLOCK))]
+    for bi in range(b):
+        for hi in range(h):
+            for r in rows:
+                x = (kn[bi, hi // g] @ qn[bi, hi, r]) * scale * np.log2(np.e)
+                if causal:
+                    x[r + 1:] = -np.inf
+                m = x.max()
+                p = np.exp2(x - m)
+                stats[bi, hi, r] = (m, p.sum())
+                out[bi, hi, r] = p @ vn[bi, hi // g] / p.sum()
+    return torch.from_numpy(out).float(), torch.from_numpy(stats).float()
+
+
+def _oracle_replay(q, k, v, row_stats, key_tiles, causal, scale, decay, window, weighted):
+    """Importance of keys in the given key tiles from every scored row, using
+    the exchanged statistics (the replay of prefill.py:61-83); zeros elsewhere."""
+    qn, kn, vn = (t.double().numpy() for t in (q, k, v))
+    st = row_stats.double().numpy()
+    b, h, n, d = qn.shape
+    hk = kn.shape[1]
+    g = h // hk
+    imp = np.zeros((b, hk, n))
+    k0, k1 = key_tiles[0] * 128, min(n, key_tiles[1] * 128)
+    w = O.recency_weights(n, decay, window, np.float64)
+    for r in range(first_scored_row(n, decay, window), n):
+        for bi in range(b):
+            for hi in range(h):
+                x = (kn[bi, hi // g, k0:k1] @ qn[bi, hi, r]) * scale * np.log2(np.e)
+                if causal:
+                    x[np.arange(k0, k1) > r] = -np.inf
+                imp[bi, hi // g, k0:k1] += w[r] * np.exp2(x - st[bi, hi, r, 0]) / st[bi, hi, r, 1]
+    if weighted:
+        imp *= np.abs(vn).sum(-1)
+    return torch.from_numpy(imp).float()
 
 
 def _oracle_select(importance, budget, recent, pool):
@@ -86,7 +120,8 @@ def _worker(rank, world, port, result_dir, mode):
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before the score all-reduce")
         out, imp, idx, mask, blocks = _query_sharded(
-            q, k, v, 64, 8, 5, True, d ** -0.5, 0.01, 0, True, True, None, _oracle_partial, _oracle_select)
+            q, k, v, 64, 8, 5, True, d ** -0.5, 0.01, 0, True, True, None, _oracle_attend, _oracle_replay,
+            _oracle_select)
         np.savez(os.path.join(result_dir, f"r{rank}.npz"), out=out.numpy(), imp=imp.numpy(), idx=idx.numpy(),
                  mask=mask.numpy(), blocks=np.array(blocks))
     except Exception as e:  # noqa: BLE001
@@ -136,3 +171,19 @@ def test_failed_rank_surfaces_as_error_not_hang(tmp_path):
     assert (tmp_path / "r1.err").exists()
     err0 = tmp_path / "r0.err"
     assert err0.exists(), "surviving rank should see its collective fail"
+
+
+@pytest.mark.parametrize("n,world", [(1, 1), (700, 2), (131072, 8), (300, 4)])
+def test_key_tile_plan_covers_all_tiles(n, world):
+    plan = key_tile_plan(n, world)
+    nkt = (n + 127) // 128
+    assert plan[0][0] == 0 and plan[-1][1] == nkt
+    for (a, b), (c, _) in zip(plan, plan[1:]):
+        assert b == c and a <= b
+    assert max(b - a for a, b in plan) - min(b - a for a, b in plan) <= 1
+
+
+def test_first_scored_row_matches_oracle():
+    for n, decay, window in [(700, 0.0, 0), (700, 0.01, 0), (131072, 0.1, 0), (8192, 0.0, 128), (100, 0.0, 500),
+                             (32768, 0.05, 4096)]:
+        assert first_scored_row(n, decay, window) == int(O.scored_rows(n, decay, window)[0])
