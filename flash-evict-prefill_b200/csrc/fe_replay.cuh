@@ -20,10 +20,10 @@
 // every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
 //
 // Roles: REPLAY_WGS reduce warpgroups (thread = key) -- warpgroup w takes
-// items w, w+WGS, w+2*WGS, ... and owns TMEM columns [128w, 128w+128) for
-// their S^T, so WGS items are reduced at once -- then the TMA producer warp
-// (K once, Q through a WGS-deep ring) and the tcgen05 issuer / TMEM owner
-// warp.  4 warpgroups with one CTA per SM, or 2 with two CTAs per SM: either
+// items w, w+WGS, w+2*WGS, ...; item i's S^T lives in TMEM buffer i % NBUF
+// (columns [128*(i % NBUF), +128)), NBUF = WGS * REPLAY_SBUF -- then the TMA
+// producer warp (K once, Q through an NBUF-deep ring) and the tcgen05 issuer /
+// TMEM owner warp.  4 warpgroups with one CTA per SM, or 2 with two CTAs per SM: either
 // way every SM sub-partition has four reduce warps to keep its MUFU busy.
 // The warpgroups' FP64 sums of a key are added in a fixed order at the end
 // (deterministic).
@@ -52,15 +52,21 @@ struct ReplayParams {
 // Exponentials per 16 evaluated by exp2_poly (FMA pipe) instead of MUFU ex2;
 // the replay is MUFU-bound (16384 exponentials per 512-cycle S^T MMA).
 constexpr int REPLAY_POLY = 2;
-// Reduce warpgroups per CTA (2 or 4): 4 with one CTA per SM, or 2 with two.
+// Reduce warpgroups per CTA and S^T buffers per warpgroup; TMEM holds
+// 4 buffers per SM, so CTAs per SM = 4 / (WGS * SBUF).  Double-buffered S^T
+// (SBUF 2: WGS 2 with one CTA per SM, or WGS 1 with two) measured 10-25 %
+// slower than 2 x 1 with two CTAs per SM: four reduce warps per SM
+// sub-partition matter more than hiding the S^T MMA behind the reduction.
 constexpr int REPLAY_WGS = 2;
+constexpr int REPLAY_SBUF = 1;
 
 template <int DP>
 struct ReplayCfg {
-  static constexpr int WGS = REPLAY_WGS;            // reduce warpgroups, one S^T buffer each
-  static constexpr int CTAS_PER_SM = 4 / WGS;       // TMEM: WGS*128 columns per CTA
+  static constexpr int WGS = REPLAY_WGS;            // reduce warpgroups
+  static constexpr int NBUF = WGS * REPLAY_SBUF;    // S^T buffers; item i uses buffer i % NBUF
+  static constexpr int CTAS_PER_SM = 4 / NBUF;      // TMEM: NBUF*128 columns per CTA
   static constexpr int TILE = 128 * DP * 2;
-  static constexpr int QST = WGS;                   // Q tile ring depth
+  static constexpr int QST = (DP <= 128) ? NBUF : 2;  // Q tile ring depth (shared memory)
   static constexpr int NCH = DP / 64;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_Q = TILE;
@@ -69,8 +75,8 @@ struct ReplayCfg {
   static constexpr int OFF_MAP = OFF_RED + WGS * 128 * 8;       // uint32 bitmap of listed query blocks
   static constexpr int MAP_WORDS = 256;                         // up to 8192 blocks
   static constexpr int OFF_BAR = OFF_MAP + MAP_WORDS * 4;
-  // k_full, q_full[QST], q_empty[QST], s_full[WGS], s_free[WGS], drain
-  static constexpr int NBAR = 1 + 2 * QST + 2 * WGS + 1;
+  // k_full, q_full[QST], q_empty[QST], s_full[NBUF], s_free[NBUF], drain
+  static constexpr int NBAR = 1 + 2 * QST + 2 * NBUF + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;
   static constexpr int PRODUCER = WGS * 4;          // warp indices
   static constexpr int ISSUER = WGS * 4 + 1;
@@ -122,8 +128,8 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + C::QST;
   uint64_t* s_full = q_empty + C::QST;
-  uint64_t* s_free = s_full + C::WGS;
-  uint64_t* drain = s_free + C::WGS;
+  uint64_t* s_free = s_full + C::NBUF;
+  uint64_t* drain = s_free + C::NBUF;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -165,7 +171,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    for (int s = 0; s < C::WGS; ++s) {
+    for (int s = 0; s < C::NBUF; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 4);
     }
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
   }
   if (warp == C::ISSUER) {
     __syncwarp();
-    tmem_alloc(tmem_holder, C::WGS * 128);
+    tmem_alloc(tmem_holder, C::NBUF * 128);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -233,10 +239,10 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
         uint32_t i = 0;
         for (; it.valid() && ok; it.next(), ++i) {
           const int s = i % C::QST;
-          const int sb = i % C::WGS;
+          const int sb = i % C::NBUF;
           ok = mbar_wait(&q_full[s], (i / C::QST) & 1, TO, abort_flag);
           if (!ok) break;
-          if (i >= C::WGS) ok = mbar_wait(&s_free[sb], ((i / C::WGS) - 1) & 1, TO, abort_flag);
+          if (i >= C::NBUF) ok = mbar_wait(&s_free[sb], ((i / C::NBUF) - 1) & 1, TO, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t qa = q_addr + s * C::TILE;
@@ -259,7 +265,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     const int kr = ((warp & 3) << 5) + static_cast<int>(lane);  // key row in tile
     const int key = kt * 128 + kr;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    const uint32_t tS = tmem + lane_off + wg * 128;
+    const uint32_t tS0 = tmem + lane_off;
     const float sc = p.sc;
     double acc = 0.0;
     ReplayItems it;
@@ -306,8 +312,12 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     for (; it.valid(); it.advance(C::WGS), ++li) {
       const int bb = li & 1;
       const float* wbias = sbias + warp * 256 + bb * 128;
+      // global item index wg + li*WGS -> S^T buffer and its use count
+      const uint32_t gi = static_cast<uint32_t>(wg) + li * C::WGS;
+      const int sb = static_cast<int>(gi % C::NBUF);
+      const uint32_t tS = tS0 + sb * 128;
       __syncwarp();  // this item's bias is written; the other buffer is free
-      ok = warp_all(mbar_wait(&s_full[wg], li & 1, TO, abort_flag));
+      ok = warp_all(mbar_wait(&s_full[sb], (gi / C::NBUF) & 1, TO, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const bool diag = p.causal && it.qt == kt;
@@ -325,7 +335,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
         if (h == 3) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[wg]);
+          if (lane == 0) mbar_arrive(&s_free[sb]);
         }
         const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 32);
 #pragma unroll
@@ -394,7 +404,7 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
   if (warp == C::ISSUER) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, C::WGS * 128);
+    tmem_dealloc(tmem, C::NBUF * 128);
   }
 }
 
