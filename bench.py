@@ -367,17 +367,21 @@ def run_ours(args, w):
     g = w["hq"] // w["hkv"]
     runs = head_unit_plan(w["b"], w["hkv"], world)[rank] if mode == "heads" else None
 
+    # One step through the public API (flash_evict.evict, or the sharded
+    # entry points); with `marks` the same body with CUDA events between the
+    # launches (prefill._evict_impl, which evict() calls).
+    def one(qq, kk, vv, marks):
+        if marks is None:
+            return evict(qq, kk, vv, budget, reserved_recent=recent, pool_kernel=pool, **kw)
+        return _evict_impl(qq, kk, vv, budget, 0, recent, pool, marks, kw)
+
     def step(qq, kk, vv, marks=None):
         if mode == "replica":
-            return _evict_impl(qq, kk, vv, budget, 0, recent, pool, marks, kw)
+            return one(qq, kk, vv, marks)
         if mode == "query":
             return evict_query_sharded(qq, kk, vv, budget, reserved_recent=recent, pool_kernel=pool, _marks=marks,
                                        **kw)
-        res = []
-        for b, h0, h1 in runs:
-            res.append(_evict_impl(qq[b:b + 1, h0 * g:h1 * g], kk[b:b + 1, h0:h1], vv[b:b + 1, h0:h1], budget, 0,
-                                   recent, pool, marks, kw))
-        return res
+        return [one(qq[b:b + 1, h0 * g:h1 * g], kk[b:b + 1, h0:h1], vv[b:b + 1, h0:h1], marks) for b, h0, h1 in runs]
 
     def barrier():
         if world > 1:

@@ -9,7 +9,6 @@ timeout, not hang.
 """
 import os
 import socket
-import sys
 
 import numpy as np
 import pytest

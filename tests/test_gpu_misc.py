@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from flash_evict import _lib, evict, prefill, select_tokens
+from flash_evict import _lib, evict, prefill
 from oracle import restate as O
 
 pytestmark = pytest.mark.gpu
