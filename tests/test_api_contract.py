@@ -72,6 +72,15 @@ def test_library_host_calls_without_gpu():
     assert rc == _lib.STATUS_OK  # nothing to gather
     rc = lib.fe_select_gather(None, 1, 1, 10, 11, 0, 1, None, None, 1, None, st, None, st, None, None, 8, 2, None)
     assert rc == _lib.STATUS_INVALID and b"budget" in lib.fe_last_error()
+    # key-tile range of the replay: 300 tokens = 3 tiles of 128 keys
+    for lo, hi in ((-1, 2), (0, 4), (2, 1)):
+        rc = lib.fe_replay_scores_range(fake, st, fake, st, fake, st, fake, fake, 1, 2, 1, 300, 64, _lib.DTYPE_BF16,
+                                        1, 0.125, 0.0, 0, 1, None, 0, lo, hi, None)
+        assert rc == _lib.STATUS_INVALID and b"key tile range" in lib.fe_last_error(), (lo, hi)
+    # an empty range is a no-op that touches nothing
+    rc = lib.fe_replay_scores_range(fake, st, fake, st, fake, st, fake, fake, 1, 2, 1, 300, 64, _lib.DTYPE_BF16,
+                                    1, 0.125, 0.0, 0, 1, None, 0, 2, 2, None)
+    assert rc == _lib.STATUS_OK
 
 
 def test_public_api_surface():
