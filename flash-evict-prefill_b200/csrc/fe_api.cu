@@ -517,18 +517,19 @@ int select_multi_impl(int64_t rows, int64_t tokens, int npol, const float* const
     if (!importance[i] || !indices[i] || !masks[i]) return fail(FE_STATUS_INVALID, "null pointer");
   int rc = bind_device(importance[0], nullptr);
   if (rc) return rc;
-  const int64_t max_slice = 49152;  // keys per CTA held in shared memory (192 KiB)
+  const int64_t max_slice = fe::SEL_SMEM_KEYS;
   // Cluster size (shared by the policies): enough CTAs for the longest past
   // region to fit in shared memory, and up to 8 for long rows (>= 4096 keys
-  // per CTA) so few rows still use many SMs.
+  // per CTA) so few rows still use many SMs.  Rows longer than 16 slices
+  // run the global-key variant (keys recomputed from the scores each pass).
   int64_t pmax = 0;
   for (int i = 0; i < npol; ++i) pmax = std::max<int64_t>(pmax, tokens - recents[i]);
   int cl = 1;
   while (cl < 16 && (pmax + cl - 1) / cl > max_slice) cl *= 2;
   while (cl < 8 && pmax / (2 * cl) >= 4096) cl *= 2;
-  if ((pmax + cl - 1) / cl > max_slice)
-    return fail(FE_STATUS_UNSUPPORTED, "sequence length %lld exceeds the selection limit (%lld)", (long long)tokens,
-                (long long)(max_slice * 16));
+  const bool smem_keys = (pmax + cl - 1) / cl <= max_slice;
+  if (pmax / cl > 0x7fffffff - fe::SEL_THREADS)
+    return fail(FE_STATUS_UNSUPPORTED, "sequence length %lld exceeds the selection limit", (long long)tokens);
   if (rows * cl * npol > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "too many rows");
   fe::SelectLaunch L;
   memset(&L, 0, sizeof(L));
@@ -553,11 +554,12 @@ int select_multi_impl(int64_t rows, int64_t tokens, int npol, const float* const
     p.gather = (g && g[i]) ? 1 : 0;
     if (p.gather) p.g = *g[i];
   }
-  const int smem = (int)(max_chunk * 4);
-  rc = set_smem(fe::fe_select_kernel, smem < 49152 ? 49152 : smem);
+  const int smem = smem_keys ? (int)(max_chunk * 4) : 0;
+  auto kern = smem_keys ? fe::fe_select_kernel<true> : fe::fe_select_kernel<false>;
+  rc = set_smem(kern, smem < 49152 ? 49152 : smem);
   if (rc) return rc;
   if (cl > 8) {
-    cudaError_t e = cudaFuncSetAttribute(fe::fe_select_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_fail(e, "cluster attribute");
   }
   cudaLaunchConfig_t cfg;
@@ -573,7 +575,7 @@ int select_multi_impl(int64_t rows, int64_t tokens, int npol, const float* const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, fe::fe_select_kernel, L);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, L);
   if (e != cudaSuccess) return cuda_fail(e, "selection launch");
   return FE_STATUS_OK;
 }

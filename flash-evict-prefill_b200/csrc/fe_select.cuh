@@ -57,6 +57,9 @@ constexpr int SEL_WARPS = SEL_THREADS / 32;
 // (flash_evict/quality_adapter.py:95-111 choose_indices per method).  All
 // policies share the launch's cluster size; each has its own slice length.
 constexpr int SEL_MAX_POLICIES = 8;
+// Keys per CTA held in shared memory (192 KiB); longer slices use the
+// global-key variant of the kernel.
+constexpr int64_t SEL_SMEM_KEYS = 49152;
 struct SelectLaunch {
   int64_t rows;  // rows per policy
   int npol;
@@ -114,6 +117,11 @@ __device__ __forceinline__ void gather_share(const SelectParams& p, cg::cluster_
   gather_rows<2>(p.g, row, out_idx, a, e - a, threadIdx.x, SEL_THREADS);
 }
 
+// SMEM_KEYS: the slice's keys are computed once into shared memory (slices of
+// up to SEL_SMEM_KEYS keys).  Otherwise (longer rows) every pass recomputes a
+// key from the scores in global memory (L2/HBM reads instead of shared
+// memory; same arithmetic, same result).
+template <bool SMEM_KEYS>
 __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_constant__ SelectLaunch L) {
   cg::cluster_group cluster = cg::this_cluster();
   const int C = static_cast<int>(cluster.num_blocks());
@@ -156,7 +164,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     // ---- keys of this slice (pooled if requested) ----
     const bool pooled = p.pool > 1;
     const int r = p.pool / 2;
-    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
+    auto key_from_scores = [&](int i) -> uint32_t {
       const int64_t gi = lo + i;
       float x;
       if (pooled) {
@@ -170,7 +178,14 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       } else {
         x = imp[gi];
       }
-      keys[i] = order_key(x);
+      return order_key(x);
+    };
+    auto key_at = [&](int i) -> uint32_t {
+      if constexpr (SMEM_KEYS) return keys[i];
+      else return key_from_scores(i);
+    };
+    if constexpr (SMEM_KEYS) {
+      for (int i = threadIdx.x; i < len; i += SEL_THREADS) keys[i] = key_from_scores(i);
     }
     for (int i = threadIdx.x; i < 512; i += SEL_THREADS) (&hist[0][0])[i] = 0;
     __syncthreads();
@@ -192,7 +207,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       // few digits, which would otherwise serialise the shared-memory atomics).
       for (int base = 0; base < len; base += SEL_THREADS) {
         const int i = base + threadIdx.x;
-        const uint32_t k = i < len ? keys[i] : 0u;
+        const uint32_t k = i < len ? key_at(i) : 0u;
         const bool match = (i < len) && ((k & pmask) == prefix);
         const uint32_t digit = match ? ((k >> shift) & 255u) : 0x100u;
         const uint32_t peers = __match_any_sync(0xffffffffu, digit);
@@ -245,7 +260,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     // ---- per-CTA counts, exchanged for offsets ----
     int gt = 0, eq = 0;
     for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
-      const uint32_t k = keys[i];
+      const uint32_t k = key_at(i);
       gt += k > T;
       eq += k == T;
     }
@@ -287,7 +302,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     for (int base = 0; base < len; base += SEL_THREADS) {
       const int i = base + threadIdx.x;
       const bool in = i < len;
-      const uint32_t k = in ? keys[i] : 0u;
+      const uint32_t k = in ? key_at(i) : 0u;
       const bool is_eq = in && (k == T);
       int tot_eq;
       const int eq_rank = block_flag_scan(is_eq, warp_sums, &tot_eq);

@@ -111,7 +111,9 @@ FE_API int fe_replay_scores_range(const void* q, const int64_t* q_strides, const
  * value first, then lower index; NaN counts as largest) together with the last
  * `recent` tokens.  indices: int64 [rows, budget], ascending.  mask: uint8
  * [rows, tokens]; with mask_evict != 0 an element is 1 when the token is
- * evicted (the reference's ~keep), else 1 when kept. */
+ * evicted (the reference's ~keep), else 1 when kept.  Any length: past
+ * regions up to 786432 tokens are held in shared memory, longer ones are
+ * re-read from `importance` on every radix pass (same result). */
 FE_API int fe_select_tokens(const float* importance, int64_t rows, int64_t tokens, int64_t budget, int64_t recent,
                      int64_t pool_kernel, int64_t* indices, uint8_t* mask, int mask_evict, void* stream);
 

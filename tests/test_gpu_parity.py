@@ -154,6 +154,27 @@ def test_long_uniform_analytic(n):
     torch.testing.assert_close(scores, expected_scores, atol=.002, rtol=.0003)
 
 
+def test_evict_one_million_tokens():
+    # Q=K=0 closed form at N = 2^20 through evict(): uniform causal attention,
+    # H2O importance = sum over q >= k of 1/(q+1); the past region is longer
+    # than the selection's shared-memory slices
+    n = 1 << 20
+    q = torch.zeros(1, 1, n, 16, device="cuda", dtype=torch.float16)
+    k = torch.zeros(1, 1, n, 16, device="cuda", dtype=q.dtype)
+    v = torch.randn(1, 1, n, 16, generator=torch.Generator().manual_seed(5)).to(q.dtype).cuda()
+    out, scores, idx, mask = evict(q, k, v, 4096, reserved_recent=64, value_weighted=False)
+    positions = torch.arange(1, n + 1, device="cuda", dtype=torch.float64)
+    rows = torch.tensor([0, 1, 4095, 777777, n - 1], device="cuda")
+    expected_out = v.double().cumsum(2)[:, :, rows] / positions[rows][None, None, :, None]
+    torch.testing.assert_close(out[:, :, rows].float(), expected_out.float(), atol=.004, rtol=.004)
+    expected = positions.reciprocal().flip(0).cumsum(0).flip(0).float()
+    torch.testing.assert_close(scores[0, 0], expected, atol=1e-6, rtol=3e-4)
+    # the scores fall with the key index: the first 4032 keys and the suffix are kept
+    _, ref_keep = O.select_tokens(scores.cpu().numpy(), 4096, reserved_recent=64)
+    np.testing.assert_array_equal((~mask).cpu().numpy(), ref_keep)
+    assert idx[0, 0, :4032].eq(torch.arange(4032, device="cuda")).all()
+
+
 @pytest.mark.parametrize("decay,window", [(.01, 0), (0., 128), (.1, 65)])
 def test_long_weighted_analytic(decay, window):
     # reference tests/test_prefill.py:134-146

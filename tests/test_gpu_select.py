@@ -65,6 +65,19 @@ def test_random_vs_oracle(rows, n, pool):
         check_exact(s, budget, recent, pool)
 
 
+@pytest.mark.parametrize("n", [786432, 786433, 1000000, 3000000])
+@pytest.mark.parametrize("pool", [1, 5])
+def test_rows_longer_than_shared_memory(n, pool):
+    # past regions above 16 x 49152 keys run the kernel variant that
+    # recomputes each key from the scores on every pass (no length limit)
+    g = torch.Generator().manual_seed(n + pool)
+    s = torch.rand((2, n), generator=g)
+    s[:, ::1000] = s[:, 7:8]  # ties across the row
+    s = s.cuda()
+    for budget, recent in ((4096, 0), (n // 10, 64)):
+        check_exact(s, budget, recent, pool)
+
+
 @pytest.mark.parametrize("n", [100, 5000, 70000])
 def test_ties_lower_index_wins(n):
     g = torch.Generator().manual_seed(n)
