@@ -406,6 +406,20 @@ int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, con
                   : launch_fwd<false, 128, 128>(tq, tk, tv, p, items, s);
 }
 
+int64_t fe_replay_first_scored_row(int64_t tokens, float recency_decay, int64_t observation_window) {
+  const int64_t W = (observation_window <= 0 || observation_window > tokens) ? tokens : observation_window;
+  int64_t s_lo = tokens - W;
+  if (recency_decay > 0) {
+    // Rows farther than this from the end have FP32 weights below 2^-127.
+    const double reach = 127.0 / ((double)recency_decay * 1.4426950408889634);
+    if (reach < (double)tokens) {
+      const int64_t cut = tokens - 1 - (int64_t)std::floor(reach);
+      if (cut > s_lo) s_lo = cut;
+    }
+  }
+  return s_lo;
+}
+
 int fe_replay_scores(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides, const void* v,
                      const int64_t* v_strides, const float* row_stats, float* importance, int64_t batch,
                      int64_t q_heads, int64_t kv_heads, int64_t tokens, int64_t channels, int dtype, int causal,
@@ -465,17 +479,7 @@ int fe_replay_scores_range(const void* q, const int64_t* q_strides, const void* 
   p.G = (int)(q_heads / kv_heads);
   p.sc = (float)((double)scale * 1.4426950408889634);
   p.decay_log2 = (float)((double)recency_decay * 1.4426950408889634);
-  const int64_t W = (observation_window == 0 || observation_window > tokens) ? tokens : observation_window;
-  int64_t s_lo = tokens - W;
-  if (recency_decay > 0) {
-    // Rows farther than this from the end have FP32 weights below 2^-127.
-    const double reach = 127.0 / ((double)recency_decay * 1.4426950408889634);
-    if (reach < (double)tokens) {
-      const int64_t cut = tokens - 1 - (int64_t)std::floor(reach);
-      if (cut > s_lo) s_lo = cut;
-    }
-  }
-  p.s_lo = (int)s_lo;
+  p.s_lo = (int)fe_replay_first_scored_row(tokens, recency_decay, observation_window);
   p.causal = causal ? 1 : 0;
   p.weighted = value_weighted ? 1 : 0;
   p.timeout_ns = (uint64_t)g_watchdog_ns;

@@ -290,7 +290,9 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
         const int c = static_cast<int>(lane) + 32 * u;
         const int q = qt * 128 + c;
         float bias = INFINITY;
-        if (q < p.N && q >= p.s_lo)
+        // l >= 1 for every attended row; a row without statistics (l <= 0 or
+        // NaN) is treated as unscored rather than producing inf.
+        if (q < p.N && q >= p.s_lo && ml[u].y > 0.f)
           bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml[u].x + lg2_approx(ml[u].y));
         dst[c] = -bias;
       }

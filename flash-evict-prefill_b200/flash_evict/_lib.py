@@ -42,6 +42,7 @@ SIGNATURES = {
                                 _INT, _INT, _F32, _VP, _I64, _VP]),
     "fe_replay_scores": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _I64, _I64, _I64, _I64, _I64,
                                 _INT, _INT, _F32, _F32, _I64, _INT, _VP, _I64, _VP]),
+    "fe_replay_first_scored_row": (_I64, [_I64, _F32, _I64]),
     "fe_replay_scores_range": (_INT, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _I64, _I64, _I64, _I64, _I64,
                                       _INT, _INT, _F32, _F32, _I64, _INT, _VP, _I64, _I64, _I64, _VP]),
     "fe_select_tokens": (_INT, [_VP, _I64, _I64, _I64, _I64, _I64, _VP, _VP, _INT, _VP]),

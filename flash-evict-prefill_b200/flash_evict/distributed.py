@@ -24,7 +24,6 @@ Each importance value is computed by one rank with the same kernel, inputs
 and summation order as on a single GPU, so the result is bitwise equal to
 single-GPU evict() for any world size.
 """
-import math
 import torch
 import torch.distributed as dist
 
@@ -77,14 +76,11 @@ def key_tile_plan(n_tokens, world):
 def first_scored_row(n_tokens, recency_decay=0.0, observation_window=0):
     """First query row that carries weight in the replay: the start of the
     observation window, raised past rows whose FP32 weight
-    exp(-decay * distance) is below 2^-127 (the rows the replay kernel skips)."""
-    w = n_tokens if observation_window == 0 or observation_window > n_tokens else observation_window
-    lo = n_tokens - w
-    if recency_decay > 0:
-        reach = 127.0 / (recency_decay * math.log2(math.e))
-        if reach < n_tokens:
-            lo = max(lo, n_tokens - 1 - int(math.floor(reach)))
-    return lo
+    exp(-decay * distance) is below 2^-127 (the rows the replay kernel skips).
+    Computed by the library itself (the kernel receives the decay as FP32), so
+    the rows exchanged here are exactly the rows the kernel reads."""
+    return int(_lib.load().fe_replay_first_scored_row(int(n_tokens), float(recency_decay),
+                                                      int(observation_window)))
 
 
 def head_unit_plan(batch, kv_heads, world):

@@ -88,6 +88,13 @@ FE_API int fe_replay_scores(const void* q, const int64_t* q_strides, const void*
                      int dtype, int causal, float scale, float recency_decay, int64_t observation_window,
                      int value_weighted, const int32_t* query_blocks, int64_t num_query_blocks, void* stream);
 
+/* First query row the replay scores for these arguments: the start of the
+ * observation window, raised past rows whose FP32 weight
+ * exp(-recency_decay * (tokens-1-q)) is below 2^-127 (skipped exactly).  A
+ * query-sharded caller exchanges the row statistics of rows >= this one.
+ * Host-only. */
+FE_API int64_t fe_replay_first_scored_row(int64_t tokens, float recency_decay, int64_t observation_window);
+
 /* fe_replay_scores restricted to the key tiles [key_tile_begin, key_tile_end)
  * (128 keys each): only importance[b, hkv, 128*key_tile_begin ..
  * 128*key_tile_end) is written, summed over all scored query rows (or the

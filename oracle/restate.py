@@ -319,7 +319,8 @@ def scored_rows(n, recency_decay=0.0, observation_window=0, skip_underflow=True)
     w_lo = n - (observation_window if observation_window and observation_window < n else n)
     lo = w_lo
     if skip_underflow and recency_decay > 0:
-        reach = 127.0 / (recency_decay * LOG2E)
+        # the kernel receives the decay as FP32
+        reach = 127.0 / (float(np.float32(recency_decay)) * LOG2E)
         if reach < n:
             lo = max(lo, n - 1 - int(math.floor(reach)))
     return np.arange(lo, n)
