@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -154,13 +155,16 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   if (rc) return rc;
   // The kernel moves registers between its warpgroups (setmaxnreg); that is
   // only safe if the launch allocation covers the split.  Refuse otherwise.
-  static int checked_regs[2][3] = {{0, 0, 0}, {0, 0, 0}};
-  int& regs = checked_regs[BF16 ? 1 : 0][DQK == 64 ? 0 : (DQK == 128 ? 1 : 2)];
+  // (one cached value per instantiation; host threads may race to fill it
+  // with the same number)
+  static std::atomic<int> checked_regs{0};
+  int regs = checked_regs.load(std::memory_order_relaxed);
   if (regs == 0) {
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
     regs = fa.numRegs;
+    checked_regs.store(regs, std::memory_order_relaxed);
   }
   if (regs < fe::FWD_REGS_NEEDED)
     return fail(FE_STATUS_UNSUPPORTED, "attention kernel compiled with %d registers/thread, needs %d", regs,
