@@ -105,7 +105,7 @@ def _oracle_select(importance, budget, recent, pool):
     return torch.from_numpy(idx), torch.from_numpy(~keep)
 
 
-def _worker(rank, world, port, result_dir, mode):
+def _worker(rank, world, port, result_dir, mode, decay=0.01, window=0):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -119,7 +119,7 @@ def _worker(rank, world, port, result_dir, mode):
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before the score all-reduce")
         out, imp, idx, mask, blocks = _query_sharded(
-            q, k, v, 64, 8, 5, True, d ** -0.5, 0.01, 0, True, True, None, _oracle_attend, _oracle_replay,
+            q, k, v, 64, 8, 5, True, d ** -0.5, decay, window, True, True, None, _oracle_attend, _oracle_replay,
             _oracle_select)
         np.savez(os.path.join(result_dir, f"r{rank}.npz"), out=out.numpy(), imp=imp.numpy(), idx=idx.numpy(),
                  mask=mask.numpy(), blocks=np.array(blocks))
@@ -133,10 +133,11 @@ def _worker(rank, world, port, result_dir, mode):
             pass
 
 
-def _spawn(mode, tmp_path):
+def _spawn(mode, tmp_path, world=2, decay=0.01, window=0):
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), mode, decay, window))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -163,6 +164,27 @@ def test_query_sharded_pipeline_gloo(tmp_path):
     ref_idx, ref_keep = O.select_tokens(ref_imp, 64, reserved_recent=8, pool_kernel=5)
     np.testing.assert_array_equal(r0["idx"], ref_idx)
     assert sorted(np.r_[r0["blocks"], r1["blocks"]].tolist()) == list(range((n + BLOCK - 1) // BLOCK))
+
+
+@pytest.mark.parametrize("world,decay,window", [(3, 0.0, 300), (4, 0.05, 0)])
+def test_query_sharded_more_ranks_than_blocks_gloo(tmp_path, world, decay, window):
+    # 700 tokens = 3 query blocks and 6 key tiles: with 4 ranks one rank owns
+    # no query block (its rows contribute nothing to the exchanges); the
+    # window starts inside a block
+    _spawn("ok", tmp_path, world, decay, window)
+    g = torch.Generator().manual_seed(0)
+    n, h, hk, d = 700, 4, 2, 32
+    q = torch.randn(1, h, n, d, generator=g)
+    k = torch.randn(1, hk, n, d, generator=g)
+    v = torch.randn(1, hk, n, d, generator=g)
+    ref_out, ref_imp = O.chunked(q, k, v, recency_decay=decay, observation_window=window)
+    res = [np.load(tmp_path / f"r{r}.npz") for r in range(world)]
+    for r in res:
+        np.testing.assert_allclose(r["imp"], ref_imp, rtol=1e-5, atol=1e-6)
+        np.testing.assert_array_equal(r["idx"], res[0]["idx"])
+    np.testing.assert_allclose(res[0]["out"], ref_out, rtol=1e-5, atol=1e-6)
+    blocks = sorted(b for r in res for b in r["blocks"].tolist())
+    assert blocks == list(range((n + BLOCK - 1) // BLOCK))
 
 
 def test_failed_rank_surfaces_as_error_not_hang(tmp_path):
