@@ -69,7 +69,7 @@ WORKLOADS = {
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # attention-forward launch, from the ncu capture in profiles/fe_fwd_kernel_c3.md.
-TRAFFIC_PER_FWD_LAUNCH = {"c3": 651232256 + 222683904}
+TRAFFIC_PER_FWD_LAUNCH = {"c3": 646584064 + 223086080}
 
 
 def peaks():
