@@ -139,6 +139,32 @@ def test_query_weighted_exact(n, decay, window, value_weighted):
     assert keep.sum(-1).eq(budget).all() and keep[..., -recent:].all()
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_normalization_counterexample_through_kernels(dtype):
+    # reference tests/test_prefill.py:62-74 through the kernels: logits
+    # [[log 9, -], [log 100, log 200]] (causal).  Normalised column sums
+    # rank key 0 first (1 + 1/3 against 2/3); unnormalised exp sums would
+    # rank key 1 first.
+    q = torch.zeros(1, 1, 2, 16)
+    k = torch.zeros(1, 1, 2, 16)
+    q[0, 0, 0, 0] = math.log(9.)
+    q[0, 0, 1, 0] = math.log(100.)
+    q[0, 0, 1, 1] = math.log(200.)
+    k[0, 0, 0, 0] = 1.
+    k[0, 0, 1, 1] = 1.
+    v = torch.ones(1, 1, 2, 16)
+    q, k, v = (t.to(dtype).cuda() for t in (q, k, v))
+    out, scores = prefill(q, k, v, scale=1.0, value_weighted=False)
+    _, ref = O.materialized(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(), scale=1.0,
+                            value_weighted=False)
+    np.testing.assert_allclose(scores.cpu().numpy(), ref, rtol=3e-4, atol=3e-5)
+    assert scores[0, 0].argmax().item() == 0
+    idx, keep = select_tokens(scores, 1)
+    assert idx.flatten().tolist() == [0]
+    logits = (q.float() @ k.float().transpose(-1, -2))[0, 0]
+    assert torch.tril(logits.exp()).sum(0).argmax().item() == 1
+
+
 @pytest.mark.parametrize("n", [8192, 32768, 131072])
 def test_long_uniform_analytic(n):
     # reference tests/test_prefill.py:88-102: Q=K=0 closed form
