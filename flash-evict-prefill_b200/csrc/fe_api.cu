@@ -54,6 +54,111 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Identity of the CUDA context current on this thread (cuCtxGetId + 1; 0 if
+// unknown).  Per-device caches below are keyed on it, so a context that was
+// destroyed and re-created (cudaDeviceReset) is set up again instead of
+// reusing addresses that belonged to the old one.
+unsigned long long current_ctx_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_cur = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  if (!get_cur || !get_id) return 0;
+  CUcontext c = nullptr;
+  if (get_cur(&c) != CUDA_SUCCESS) return 0;
+  if (c == nullptr) {
+    // No context bound to this thread yet: cudaSetDevice creates (or binds)
+    // the device's primary context.
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || cudaSetDevice(d) != cudaSuccess) return 0;
+    if (get_cur(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+  }
+  unsigned long long id = 0;
+  if (get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id + 1;
+}
+
+// ------------------------------------------------ host-visible status word --
+// Kernels that give up on a wait (watchdog) raise the device status word and,
+// once the library has attached it, also write the code into this device's
+// word of a mapped pinned host array.  Every compute entry point reads that
+// word on entry (plain host memory, no synchronization): a code left there by
+// an earlier call's kernel is returned as that call's error and cleared, so an
+// asynchronous failure surfaces at the caller's next call on the device.
+constexpr int kMaxDevices = 64;
+std::mutex g_status_mu;
+int* g_status_words = nullptr;                        // [kMaxDevices], mapped pinned host memory
+unsigned long long g_status_ctx[kMaxDevices] = {0};  // context the word was attached in
+thread_local bool g_no_attach = false;                 // set inside the allocation-free entry point
+
+__global__ void fe_attach_status_kernel(int* word) { fe::g_status_host = word; }
+
+// Attach `dev`'s host word for the current context: allocate the pinned array
+// once per process (the only allocation this library makes on its own) and
+// publish the word's address to the device with a one-thread kernel on the
+// caller's stream (stream-ordered before the caller's kernels).  Skipped
+// while the stream is being captured; a later uncaptured call attaches.
+int attach_status(int dev, void* stream) {
+  if (dev < 0 || dev >= kMaxDevices || g_no_attach) return FE_STATUS_OK;
+  const unsigned long long ctx = current_ctx_id();
+  if (ctx == 0) return FE_STATUS_OK;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if (g_status_ctx[dev] == ctx) return FE_STATUS_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return FE_STATUS_OK;
+  if (g_status_words == nullptr) {
+    // Relaxed capture mode for this one allocation, in case another thread
+    // of the process is capturing a graph in global mode.
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    void* h = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, kMaxDevices * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc (status words)");
+    memset(h, 0, kMaxDevices * sizeof(int));
+    g_status_words = static_cast<int*>(h);
+  }
+  int* dptr = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dptr), g_status_words + dev, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer (status word)");
+  fe_attach_status_kernel<<<1, 1, 0, s>>>(dptr);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "status attach launch");
+  g_status_ctx[dev] = ctx;
+  return FE_STATUS_OK;
+}
+
+const char* status_name(int code) {
+  switch (code) {
+    case FE_STATUS_TIMEOUT: return "device watchdog timeout";
+    case FE_STATUS_BAD_INDEX: return "gather index out of range";
+    default: return "device error";
+  }
+}
+
+// Take (read and clear) a status code that an earlier call's kernel left in
+// `dev`'s host word; non-zero codes become this call's error.
+int take_pending(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return FE_STATUS_OK;
+  int* words = __atomic_load_n(&g_status_words, __ATOMIC_ACQUIRE);
+  if (words == nullptr) return FE_STATUS_OK;
+  const int code = __atomic_exchange_n(words + dev, 0, __ATOMIC_ACQ_REL);
+  if (code == FE_STATUS_OK) return FE_STATUS_OK;
+  return fail(code, "a kernel launched by an earlier call on device %d stopped: %s (its outputs are NaN where "
+              "the kernel could mark them, otherwise undefined); this call launched nothing", dev, status_name(code));
+}
+
 // Make the device owning `ptr` current for this runtime instance.
 int bind_device(const void* ptr, int* dev_out) {
   cudaPointerAttributes a;
@@ -68,6 +173,18 @@ int bind_device(const void* ptr, int* dev_out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   }
   if (dev_out) *dev_out = a.device;
+  return FE_STATUS_OK;
+}
+
+// Entry of a compute call: bind the device owning `ptr`, report a status an
+// earlier call's kernel raised, and attach the host status word if needed.
+int enter(const void* ptr, void* stream, int* dev_out = nullptr) {
+  int dev = 0;
+  int rc = bind_device(ptr, &dev);
+  if (rc) return rc;
+  if ((rc = take_pending(dev))) return rc;
+  if ((rc = attach_status(dev, stream))) return rc;
+  if (dev_out) *dev_out = dev;
   return FE_STATUS_OK;
 }
 
@@ -333,13 +450,13 @@ __global__ void fe_exp2_selftest_kernel(const float* in, float* poly, float* muf
 
 extern "C" {
 
-int fe_abi_version(void) { return 2; }
+int fe_abi_version(void) { return 3; }
 
 int fe_selftest_exp2(const float* in, float* out_poly, float* out_mufu, int64_t n, void* stream) {
   g_err[0] = 0;
   if (n < 0 || (n > 0 && (!in || !out_poly || !out_mufu))) return fail(FE_STATUS_INVALID, "bad arguments");
   if (n == 0) return FE_STATUS_OK;
-  int rc = bind_device(in, nullptr);
+  int rc = enter(in, stream);
   if (rc) return rc;
   const int64_t blocks = (n + 255) / 256;
   if (blocks > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "n too large");
@@ -364,7 +481,7 @@ int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, con
   if (!q || !k || !v || !out || !row_stats) return fail(FE_STATUS_INVALID, "null pointer");
   if (!std::isfinite(scale)) return fail(FE_STATUS_INVALID, "scale must be finite");
   if (reinterpret_cast<uintptr_t>(out) % 16) return fail(FE_STATUS_UNSUPPORTED, "out must be 16-byte aligned");
-  rc = bind_device(q, nullptr);
+  rc = enter(q, stream);
   if (rc) return rc;
   CUtensorMap tq, tk, tv;
   if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q"))) return rc;
@@ -454,7 +571,7 @@ int fe_replay_scores_range(const void* q, const int64_t* q_strides, const void* 
     return fail(FE_STATUS_INVALID, "recency_decay must be finite and nonnegative");
   if (observation_window < 0) return fail(FE_STATUS_INVALID, "observation_window must be >= 0");
   if (v_strides[3] != 1) return fail(FE_STATUS_UNSUPPORTED, "v: channel stride must be 1");
-  rc = bind_device(q, nullptr);
+  rc = enter(q, stream);
   if (rc) return rc;
   CUtensorMap tq, tk;
   if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q"))) return rc;
@@ -523,7 +640,7 @@ int select_multi_impl(int64_t rows, int64_t tokens, int npol, const float* const
   if (rows == 0) return FE_STATUS_OK;
   for (int i = 0; i < npol; ++i)
     if (!importance[i] || !indices[i] || !masks[i]) return fail(FE_STATUS_INVALID, "null pointer");
-  int rc = bind_device(importance[0], nullptr);
+  int rc = enter(importance[0], stream);
   if (rc) return rc;
   const int64_t max_slice = fe::SEL_SMEM_KEYS;
   // Cluster size (shared by the policies): enough CTAs for the longest past
@@ -619,7 +736,7 @@ int fe_gather_tokens(const void* k, const int64_t* k_strides, const void* v, con
   int rc = make_gather_spec(&g, k, k_strides, v, v_strides, k_out, v_out, batch, heads, tokens, budget, channels,
                             elem_bytes);
   if (rc) return rc;
-  rc = bind_device(k, nullptr);
+  rc = enter(k, stream);
   if (rc) return rc;
   const int64_t per_row = (budget + fe::GATHER_POSITIONS - 1) / fe::GATHER_POSITIONS;
   const int64_t blocks = per_row * batch * heads;
@@ -733,7 +850,7 @@ int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k, const
   if (workspace_floats < g.workspace_floats)
     return fail(FE_STATUS_INVALID, "workspace too small: %lld floats needed", (long long)g.workspace_floats);
   if (reinterpret_cast<uintptr_t>(workspace) % 8) return fail(FE_STATUS_INVALID, "workspace must be 8-byte aligned");
-  rc = bind_device(q, nullptr);
+  rc = enter(q, stream);
   if (rc) return rc;
   CUtensorMap tq, tk;
   if ((rc = make_map(&tq, q, q_strides, batch, q_heads, tokens, channels, dtype, "q", g.box))) return rc;
@@ -781,6 +898,10 @@ int fe_device_status(int device, int clear, int* status_out) {
   if (e == cudaSuccess && clear) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(fe::g_status, &zero, sizeof(int));
+    // The device is idle, so the host word holds its final value: clear it
+    // too, so the next call does not report what was just read here.
+    int* words = __atomic_load_n(&g_status_words, __ATOMIC_ACQUIRE);
+    if (words != nullptr && device >= 0 && device < kMaxDevices) __atomic_store_n(words + device, 0, __ATOMIC_RELEASE);
   }
   if (cur >= 0 && cur != device) cudaSetDevice(cur);
   if (e != cudaSuccess) return cuda_fail(e, "status read");
@@ -791,6 +912,11 @@ int fe_device_status(int device, int clear, int* status_out) {
 int fe_watchdog_selftest(int64_t timeout_ns, void* stream) {
   g_err[0] = 0;
   if (timeout_ns <= 0 || timeout_ns > 10000000000LL) return fail(FE_STATUS_INVALID, "timeout out of range");
+  int dev = 0;
+  cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) return cuda_fail(e0, "cudaGetDevice");
+  int rc = attach_status(dev, stream);
+  if (rc) return rc;
   fe_watchdog_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)timeout_ns);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "watchdog launch");
@@ -820,24 +946,38 @@ constexpr int64_t kNoAllocMaxRows = int64_t(1) << 22;  // batch*q_heads*tokens r
 
 static __device__ __align__(256) float2 fe_noalloc_row_stats[kNoAllocMaxRows];
 
-// Device address of fe_noalloc_row_stats on each device, looked up once.
+// Device address of fe_noalloc_row_stats on each device, looked up once per
+// device and context (a context created anew after cudaDeviceReset has its
+// own copy of the array, so the address is looked up again).
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {nullptr};
+void* g_noalloc_ptr[kMaxDevices] = {nullptr};
+unsigned long long g_noalloc_ctx[kMaxDevices] = {0};
 
 int noalloc_scratch(int dev, float** out) {
-  if (dev < 0 || dev >= 64) return fail(FE_STATUS_UNSUPPORTED, "fe_evict_noalloc: device index %d out of range", dev);
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(FE_STATUS_UNSUPPORTED, "fe_evict_noalloc: device index %d out of range", dev);
+  const unsigned long long ctx = current_ctx_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc_ptr[dev] == nullptr || ctx == 0 || g_noalloc_ctx[dev] != ctx) {
     // The caller's device is current here (bind_device); the symbol's host
     // name is only a stand-in, so ask the runtime for its device address.
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, fe_noalloc_row_stats);
     if (e != cudaSuccess) return cuda_fail(e, "fe_evict_noalloc: cudaGetSymbolAddress");
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = static_cast<float*>(g_noalloc_ptr[dev]);
   return FE_STATUS_OK;
 }
+
+// Keeps the entry points called by fe_evict_noalloc from attaching the host
+// status word (which allocates pinned host memory) on this thread.
+struct NoAttachScope {
+  bool prev;
+  NoAttachScope() : prev(g_no_attach) { g_no_attach = true; }
+  ~NoAttachScope() { g_no_attach = prev; }
+};
 
 }  // namespace
 
@@ -864,7 +1004,11 @@ extern "C" int fe_evict_noalloc(const void* q, const int64_t* q_strides, const v
   rc = noalloc_scratch(dev, &scratch);
   if (rc) return rc;
   // Every row the replay reads is written by the attention kernel earlier on
-  // the same stream, so the scratch needs no clearing between calls.
+  // the same stream (valid statistics, or NaN when that kernel gave up on a
+  // wait), so the scratch needs no clearing between calls.  The host status
+  // word is used when an earlier call of another entry point attached it;
+  // this entry point never attaches it itself (that allocates).
+  NoAttachScope no_attach;
   return fe_evict(q, q_strides, k, k_strides, v, v_strides, out, importance, indices, mask, scratch, batch, q_heads,
                   kv_heads, tokens, channels, dtype, causal, scale, recency_decay, observation_window, value_weighted,
                   budget, recent, pool_kernel, stream);

@@ -432,9 +432,22 @@ __global__ void __launch_bounds__(384, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
     }
+    if (nt > 0 && ok) ok = warp_all(mbar_wait(&o_full[t], 0, TO, abort_flag));
+    if (nt > 0 && !ok && row < p.N) {
+      // Aborted (watchdog): mark this row's statistics and output channels
+      // as NaN so that nothing downstream (the replay, a caller reading the
+      // output) mistakes stale memory for a result.
+      if (p.vcol0 == 0) {
+        float2* st = reinterpret_cast<float2*>(p.row_stats) + (static_cast<size_t>(b) * p.Hq + hq) * p.N + row;
+        *st = make_float2(__int_as_float(0x7fffffff), __int_as_float(0x7fffffff));
+      }
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = reinterpret_cast<T*>(p.out) + ((static_cast<size_t>(b) * p.Hq + hq) * p.N + row) * p.D + p.vcol0;
+      const uint16_t nan16 = BF16 ? 0x7fc0 : 0x7e00;
+      for (int c = 0; c < DV && c < p.D - p.vcol0; ++c) reinterpret_cast<uint16_t*>(orow)[c] = nan16;
+    }
     if (nt > 0 && ok) {
-      ok = warp_all(mbar_wait(&o_full[t], 0, TO, abort_flag));
-      if (ok) {
+      {
         tc_fence_after();
         const bool live = row < p.N;
         if (live && p.vcol0 == 0) {

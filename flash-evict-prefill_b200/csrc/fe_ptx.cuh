@@ -21,8 +21,19 @@ namespace fe {
 // is one translation unit (fe_api.cu includes every kernel header), so the
 // definition lives here.
 __device__ int g_status = 0;
+// This device's word in mapped pinned host memory (null until the library
+// attaches it): a raised status is also written there, so the host sees it at
+// its next call without synchronizing the device.
+__device__ int* g_status_host = nullptr;
 
-__device__ __forceinline__ void raise_status(int code) { atomicMax(&g_status, code); }
+__device__ __forceinline__ void raise_status(int code) {
+  atomicMax(&g_status, code);
+  volatile int* h = *const_cast<int* volatile*>(&g_status_host);
+  if (h != nullptr) {
+    if (*h < code) *h = code;
+    __threadfence_system();
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -290,9 +290,12 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
         const int c = static_cast<int>(lane) + 32 * u;
         const int q = qt * 128 + c;
         float bias = INFINITY;
-        // l >= 1 for every attended row; a row without statistics (l <= 0 or
-        // NaN) is treated as unscored rather than producing inf.
-        if (q < p.N && q >= p.s_lo && ml[u].y > 0.f)
+        // l >= 1 for every attended row; a row without statistics (l == 0,
+        // the zeros a query-sharded rank holds for rows it did not compute)
+        // is treated as unscored rather than producing inf.  NaN statistics
+        // (an aborted attention launch) give a NaN bias, which poisons every
+        // key the row reaches.
+        if (q < p.N && q >= p.s_lo && !(ml[u].y <= 0.f))
           bias = fmaf(-p.decay_log2, static_cast<float>(q - (p.N - 1)), ml[u].x + lg2_approx(ml[u].y));
         dst[c] = -bias;
       }
@@ -379,7 +382,11 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     // Combine the four warpgroups' sums of each key in a fixed order.
     sred[wg * 128 + kr] = acc;
     named_bar_sync(1, C::WGS * 128);
-    if (wg == 0 && !*abort_flag && key < p.N) {
+    if (wg == 0 && key < p.N && *abort_flag) {
+      // Aborted (watchdog): the sums are incomplete; store NaN, never a
+      // plausible-looking partial value.
+      p.importance[(static_cast<size_t>(b) * p.Hkv + hkv) * p.N + key] = __int_as_float(0x7fffffff);
+    } else if (wg == 0 && key < p.N) {
       double total = sred[kr];
 #pragma unroll
       for (int w = 1; w < C::WGS; ++w) total += sred[w * 128 + kr];

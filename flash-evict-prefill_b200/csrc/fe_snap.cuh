@@ -305,9 +305,12 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-    if (ok) {
+    {
+      // On an abort (watchdog) the partial sums are NaN, which the scoring
+      // pass turns into NaN scores instead of using stale workspace.
+      const float nan = __int_as_float(0x7fffffff);
       float2* dst = p.partial + ((static_cast<size_t>(bh) * p.groups + grp) * p.nchunk + chunk) * 256;
-      for (int m = 0; m < MT; ++m) dst[m * 128 + row] = make_float2(mrun[m], lrun[m]);
+      for (int m = 0; m < MT; ++m) dst[m * 128 + row] = ok ? make_float2(mrun[m], lrun[m]) : make_float2(nan, nan);
     }
   }
 
@@ -508,8 +511,9 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
     // mean over the G heads of the KV head, as the reference's mean(2)
-    if (ok && key < p.N)
-      p.scores[static_cast<size_t>(bh) * p.N + key] = __fdiv_rn(static_cast<float>(acc), static_cast<float>(p.G));
+    if (key < p.N)
+      p.scores[static_cast<size_t>(bh) * p.N + key] =
+          ok ? __fdiv_rn(static_cast<float>(acc), static_cast<float>(p.G)) : __int_as_float(0x7fffffff);
   }
 
   tc_fence_before();

@@ -97,6 +97,10 @@ def strides(t):
     return (ctypes.c_int64 * 4)(*t.stride())
 
 
+def status_name(code):
+    return _STATUS_NAMES.get(code, f"status {code}")
+
+
 def check(rc):
     if rc != STATUS_OK:
         msg = load().fe_last_error().decode(errors="replace")

@@ -53,7 +53,7 @@ def test_header_constants_match_binding():
 
 def test_library_host_calls_without_gpu():
     lib = _lib.load()
-    assert lib.fe_abi_version() == 2
+    assert lib.fe_abi_version() == 3
     # argument checks run on the host before any device work
     rc = lib.fe_select_tokens(None, 1, 10, 0, 0, 1, None, None, 1, None)
     assert rc == _lib.STATUS_INVALID
@@ -85,7 +85,7 @@ def test_library_host_calls_without_gpu():
 
 def test_public_api_surface():
     assert flash_evict.__all__[:3] == ["prefill", "evict", "select_tokens"]
-    assert set(flash_evict.__all__[3:]) == {"gather_tokens", "select_and_gather", "evict_compact"}
+    assert set(flash_evict.__all__[3:]) == {"gather_tokens", "select_and_gather", "evict_compact", "check_status"}
     import inspect
     sig = inspect.signature(prefill)
     assert list(sig.parameters) == ["q", "k", "v", "causal", "value_weighted", "score", "scale", "block_q",
