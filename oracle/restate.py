@@ -324,3 +324,59 @@ def scored_rows(n, recency_decay=0.0, observation_window=0, skip_underflow=True)
         if reach < n:
             lo = max(lo, n - 1 - int(math.floor(reach)))
     return np.arange(lo, n)
+
+
+def parity_figures(out_got, out_ref, imp_got, imp_ref, rel_floor=1e-6):
+    """Error figures of a GPU result against this oracle (float64 truth).
+
+    out_got/out_ref: sampled attention-output rows (any matching shape).
+    imp_got/imp_ref: importance [..., N].  The relative importance error is
+    taken over keys whose reference importance is at least `rel_floor` times
+    the largest of its row (smaller ones sit at the FP32 underflow edge of
+    exp2, where a relative figure means nothing); their absolute error is
+    reported relative to that row maximum instead.
+    """
+    og = np.asarray(out_got, dtype=np.float64)
+    orf = np.asarray(out_ref, dtype=np.float64)
+    ig = np.asarray(imp_got, dtype=np.float64).reshape(-1, np.asarray(imp_got).shape[-1])
+    ir = np.asarray(imp_ref, dtype=np.float64).reshape(ig.shape)
+    err = np.abs(ig - ir)
+    rowmax = np.maximum(np.abs(ir).max(-1, keepdims=True), 1e-300)
+    big = np.abs(ir) >= rel_floor * rowmax
+    rel = np.where(big, err / np.maximum(np.abs(ir), 1e-300), 0.0)
+    return {
+        "out_max_abs": float(np.abs(og - orf).max()) if og.size else 0.0,
+        "out_max_rel": float(np.abs(og - orf).max() / max(np.abs(orf).max(), 1e-300)) if og.size else 0.0,
+        "importance_max_rel": float(rel.max()),
+        "importance_rel_floor": rel_floor,
+        "importance_keys_checked": int(big.sum()),
+        "importance_small_max_abs_over_rowmax": float((np.where(big, 0.0, err) / rowmax).max()),
+        "importance_nonfinite": int((~np.isfinite(ig)).sum()),
+    }
+
+
+def selection_figures(keep_got, imp_ref, budget, *, recent=0, reserved_recent=None, pool_kernel=1, tie_rtol=1e-5):
+    """Keep-mask differences between a GPU selection and this oracle's
+    selection on the reference importance, and how many of the differing
+    tokens are near ties: their reference selection score (the pooled past
+    score when pool_kernel > 1) lies within tie_rtol (relative) of the row's
+    threshold, the smallest reference score that was kept."""
+    imp = np.asarray(imp_ref, dtype=np.float32)
+    n = imp.shape[-1]
+    recent = _check_select_args(n, budget, recent, reserved_recent, pool_kernel)
+    _, ref_keep = select_tokens(imp, budget, recent=recent, pool_kernel=pool_kernel)
+    got = np.asarray(keep_got, dtype=bool).reshape(-1, n)
+    ref_keep = ref_keep.reshape(-1, n)
+    past = imp.reshape(-1, n)[:, :n - recent]
+    if pool_kernel > 1 and budget > recent:
+        past = avg_pool(past, pool_kernel)
+    diff = got != ref_keep
+    ties = 0
+    for r in np.nonzero(diff.any(1))[0]:
+        kept = past[r][ref_keep[r, :n - recent]]
+        thr = float(kept.min()) if kept.size else 0.0
+        for c in np.nonzero(diff[r])[0]:
+            if c < n - recent and abs(float(past[r, c]) - thr) <= tie_rtol * abs(thr):
+                ties += 1
+    return {"mask_mismatches": int(diff.sum()), "mismatches_near_ties": ties, "tie_rtol": tie_rtol,
+            "index_rows_equal": int((~diff.any(1)).sum()), "rows": int(diff.shape[0])}

@@ -80,3 +80,15 @@ def selection_mismatch(keep, ref_keep, scores, ref_scores, tol_abs, tol_rel):
             if abs(ref_scores[r, c] - thr) > tol_abs + tol_rel * abs(thr):
                 ok = False
     return mism, ok
+
+
+# Parity figures recorded by the GPU tests (one line per configuration),
+# printed in the terminal summary by conftest.py.
+PARITY_FIGURES = []
+
+
+def record_figures(name, figs):
+    keys = ("out_max_abs", "out_max_rel", "importance_max_rel", "importance_keys_checked", "mask_mismatches",
+            "mismatches_near_ties")
+    PARITY_FIGURES.append(name + ": " + ", ".join(f"{k}={figs[k]:.3g}" if isinstance(figs[k], float)
+                                                 else f"{k}={figs[k]}" for k in keys if k in figs))

@@ -46,3 +46,11 @@ def _device_status(request):
             from flash_evict import _lib
             status = _lib.device_status(torch.cuda.current_device(), clear=True)
             assert status == 0, f"device status word raised: {status}"
+
+
+def pytest_terminal_summary(terminalreporter):
+    from common import PARITY_FIGURES
+    if PARITY_FIGURES:
+        terminalreporter.write_sep("-", "parity figures (GPU vs float64 oracle)")
+        for line in PARITY_FIGURES:
+            terminalreporter.write_line(line)

@@ -1,6 +1,7 @@
-"""GPU: determinism, layouts, the C ABI called directly, the watchdog path,
-and parity at the BASELINE configurations (full sizes, sampled oracle rows
-plus size-independent properties)."""
+"""GPU: determinism, layouts, the C ABI called directly, the watchdog path
+(timeouts raised at the caller's next call, NaN poisoning), the exp2
+polynomial and CUDA-graph capture.  Parity at the BASELINE configurations is
+in test_gpu_parity_configs.py."""
 import ctypes
 
 import numpy as np
@@ -89,6 +90,80 @@ def test_watchdog_timeout_is_reported_not_hung():
     assert torch.isfinite(out.float()).all()
 
 
+def _watchdog_trip(dev):
+    """Launch the self-test kernel whose wait nothing satisfies (2 ms limit)
+    and wait for it, so its status is in the host word when the next call
+    enters the library."""
+    lib = _lib.load()
+    _lib.check(lib.fe_watchdog_selftest(2_000_000, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize(dev)
+
+
+def test_watchdog_timeout_raises_at_next_call_then_clears():
+    # An asynchronous kernel failure reaches the Python caller: the next call
+    # on the device raises RuntimeError (and launches nothing), the call
+    # after it runs normally and gives the same bits as before the failure.
+    from flash_evict import check_status
+    dev = torch.cuda.current_device()
+    assert _lib.device_status(dev, clear=True) == 0
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(1, 4, 700, 64, generator=g).to(torch.float16).cuda()
+    k = torch.randn(1, 2, 700, 64, generator=g).to(torch.float16).cuda()
+    v = torch.randn(1, 2, 700, 64, generator=g).to(torch.float16).cuda()
+    ref = evict(q, k, v, 64, reserved_recent=8)
+    torch.cuda.synchronize()
+    _watchdog_trip(dev)
+    with pytest.raises(RuntimeError, match="device watchdog timeout"):
+        evict(q, k, v, 64, reserved_recent=8)
+    got = evict(q, k, v, 64, reserved_recent=8)
+    torch.cuda.synchronize()
+    for a, b_ in zip(got, ref):
+        assert torch.equal(a, b_)
+    # the synchronous check still sees the device record once, then clears it
+    with pytest.raises(RuntimeError, match="device watchdog timeout"):
+        check_status(dev)
+    check_status(dev)
+
+
+def test_check_status_reports_without_a_later_call():
+    from flash_evict import check_status
+    dev = torch.cuda.current_device()
+    check_status()
+    _watchdog_trip(dev)
+    with pytest.raises(RuntimeError, match="device watchdog timeout"):
+        check_status(torch.device("cuda", dev))
+    check_status(dev)
+    # the host word was cleared with the device word: the next call runs
+    x = torch.randn(1, 1, 64, 64, device="cuda", dtype=torch.float16)
+    prefill(x, x, x)
+    check_status()
+
+
+def test_replay_poisons_keys_reached_by_nan_row_statistics():
+    # What an aborted attention launch leaves behind (NaN {m, l} for its
+    # rows) makes the replay write NaN importance for every key those rows
+    # attend to, instead of a plausible partial sum.
+    from flash_evict.prefill import _attention, _replay
+    g = torch.Generator().manual_seed(8)
+    n = 600
+    q = torch.randn(1, 4, n, 64, generator=g).to(torch.bfloat16).cuda()
+    k = torch.randn(1, 2, n, 64, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(1, 2, n, 64, generator=g).to(torch.bfloat16).cuda()
+    out = torch.empty_like(q)
+    stats = torch.empty(1, 4, n, 2, device="cuda")
+    _attention(q, k, v, out, stats, True, 64 ** -0.5)
+    imp_ok = torch.empty(1, 2, n, device="cuda")
+    _replay(q, k, v, stats, imp_ok, True, 64 ** -0.5, 0.0, 0, True)
+    stats[0, 1, 300] = float("nan")       # query head 1 -> kv head 0, row 300
+    imp = torch.empty(1, 2, n, device="cuda")
+    _replay(q, k, v, stats, imp, True, 64 ** -0.5, 0.0, 0, True)
+    torch.cuda.synchronize()
+    assert torch.isnan(imp[0, 0, :301]).all()           # keys row 300 attends to (causal)
+    assert torch.equal(imp[0, 0, 301:], imp_ok[0, 0, 301:])
+    assert torch.equal(imp[0, 1], imp_ok[0, 1])          # the other kv head is untouched
+    assert torch.isfinite(imp_ok).all()
+
+
 def test_head_dim_above_256_is_rejected():
     # the reference's contract (prefill.py:95-96): head dimension <= 256
     x = torch.randn(1, 1, 64, 264, device="cuda", dtype=torch.float16)
@@ -101,83 +176,6 @@ def test_head_dim_above_256_is_rejected():
                               _lib.strides(x), y.data_ptr(), st.data_ptr(), 1, 1, 1, 64, 264, _lib.DTYPE_F16, 1,
                               ctypes.c_float(0.06), None, 0, torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.STATUS_INVALID and b"256" in lib.fe_last_error()
-
-
-# --------------------------------------------------------- BASELINE configs --
-
-def _gen(shape, seed, dtype, scale=1.0):
-    g = torch.Generator().manual_seed(seed)
-    return (torch.randn(shape, generator=g) * scale).to(dtype)
-
-
-def _check_config(q, k, v, budget, sample_rows, out_tol, imp_rtol, imp_atol, **kw):
-    causal = kw.pop("causal", True)
-    pool = kw.pop("pool_kernel", 1)
-    recent = kw.pop("reserved_recent", 0)
-    out, imp, idx, mask = evict(q, k, v, budget, causal=causal, pool_kernel=pool, reserved_recent=recent, **kw)
-    torch.cuda.synchronize()
-    n = q.shape[2]
-    ref_out, ref_imp = O.chunked(q.cpu(), k.cpu(), v.cpu(), causal=causal, out_rows=sample_rows,
-                                 recency_decay=kw.get("recency_decay", 0.0),
-                                 observation_window=kw.get("observation_window", 0),
-                                 value_weighted=kw.get("value_weighted", True), weight_floor=1e-30)
-    got = out[:, :, sample_rows].float().cpu().numpy()
-    np.testing.assert_allclose(got, ref_out[:, :, sample_rows], atol=out_tol, rtol=0.006)
-    np.testing.assert_allclose(imp.cpu().numpy(), ref_imp, atol=imp_atol, rtol=imp_rtol)
-    ref_idx, ref_keep = O.select_tokens(ref_imp, budget, reserved_recent=recent, pool_kernel=pool)
-    from common import selection_mismatch
-    mism, ok = selection_mismatch(~mask.cpu().numpy(), ref_keep, imp.cpu().numpy(), ref_imp, imp_atol, imp_rtol)
-    assert ok, mism
-    assert (~mask).sum(-1).eq(budget).all()
-    return mism
-
-
-def test_config2_llama_8k():
-    # B1 Hq32 Hkv8 N8192 D128 bf16 causal, q,k ~ N(0,1)/D^0.25, decay 0.1, reserved 64, budget 1024
-    n, d = 8192, 128
-    q = (_gen((1, 32, n, d), 0, torch.float32) / d ** 0.25).to(torch.bfloat16).cuda()
-    k = (_gen((1, 8, n, d), 1, torch.float32) / d ** 0.25).to(torch.bfloat16).cuda()
-    v = _gen((1, 8, n, d), 2, torch.bfloat16).cuda()
-    rows = np.unique(np.r_[0, 1, 127, 128, 4095, n - 1, np.random.default_rng(0).integers(0, n, 24)])
-    _check_config(q, k, v, 1024, rows, 0.012, 1e-4, 1e-6, recency_decay=0.1, reserved_recent=64)
-
-
-def test_config3_qwen_32k():
-    # B1 Hq28 Hkv4 N32768 D128 fp16 causal, 1% of k rows x8, window 128, pool 5, budget 2048
-    n, d = 32768, 128
-    q = _gen((1, 28, n, d), 0, torch.float16).cuda()
-    k = _gen((1, 4, n, d), 1, torch.float32)
-    sink = torch.randperm(n, generator=torch.Generator().manual_seed(3))[: n // 100]
-    k[:, :, sink] *= 8
-    k = k.to(torch.float16).cuda()
-    v = _gen((1, 4, n, d), 2, torch.float16).cuda()
-    rows = np.unique(np.r_[0, 255, 256, n - 129, n - 1, np.random.default_rng(1).integers(0, n, 12)])
-    _check_config(q, k, v, 2048, rows, 0.002, 3e-4, 3e-3, observation_window=128, pool_kernel=5)
-
-
-def test_config5_batched_mha_noncausal_h2o_sampled():
-    # B8 Hq=Hkv=32 N4096 D128 fp16 noncausal, [B,N,H,D] strides, q x30, 5% zero v rows, H2O, budget 410
-    b, h, n, d = 8, 32, 4096, 128
-    q = (_gen((b, n, h, d), 0, torch.float32) * 30).to(torch.float16).cuda().transpose(1, 2)
-    k = _gen((b, n, h, d), 1, torch.float16).cuda().transpose(1, 2)
-    v = _gen((b, n, h, d), 2, torch.float32)
-    zero = torch.randperm(n, generator=torch.Generator().manual_seed(4))[: n * 5 // 100]
-    v[:, zero] = 0
-    v = v.to(torch.float16).cuda().transpose(1, 2)
-    out, imp, idx, mask = evict(q, k, v, 410, causal=False, value_weighted=False)
-    torch.cuda.synchronize()
-    # size-independent: H2O mass of each (b, h) sums to N (noncausal softmax rows sum to 1)
-    torch.testing.assert_close(imp.double().sum(-1), torch.full((b, h), float(n), dtype=torch.float64,
-                                                                device="cuda"), rtol=1e-5, atol=1e-3)
-    # exact oracle on a few (b, h) units
-    for bi, hi in ((0, 0), (3, 17), (7, 31)):
-        sl = slice(hi, hi + 1)
-        rows = np.r_[0, 1, 2047, n - 1]
-        ro, ri = O.chunked(q[bi:bi + 1, sl].cpu(), k[bi:bi + 1, sl].cpu(), v[bi:bi + 1, sl].cpu(), causal=False,
-                           value_weighted=False, out_rows=rows)
-        np.testing.assert_allclose(out[bi, hi, rows].float().cpu().numpy(), ro[0, 0, rows], atol=0.004, rtol=0.006)
-        np.testing.assert_allclose(imp[bi, hi].cpu().numpy(), ri[0, 0], atol=1e-3, rtol=1e-3)
-    assert (~mask).sum(-1).eq(410).all()
 
 
 def test_exp2_polynomial_error_bound():

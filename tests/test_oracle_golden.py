@@ -150,3 +150,37 @@ def test_round_to_dtype_matches_torch():
     x = (torch.randn(10000, generator=torch.Generator().manual_seed(2)) * 300).float()
     for name, dt in (("float16", torch.float16), ("bfloat16", torch.bfloat16)):
         np.testing.assert_array_equal(O.round_to_dtype(x.numpy(), name), x.to(dt).float().numpy())
+
+
+def test_parity_and_selection_figures_helpers():
+    # The figure helpers the GPU parity tests and bench.py report with.
+    ref = np.array([[4.0, 3.0, 2.0, 1.0, 1e-12, 0.5]], dtype=np.float64)
+    got = ref * (1 + np.array([[1e-6, -2e-6, 0, 0, 0.5, 3e-6]]))
+    f = O.parity_figures(np.ones(3), np.ones(3) * 1.001, got, ref, rel_floor=1e-9)
+    assert abs(f["importance_max_rel"] - 3e-6) < 1e-12
+    assert f["importance_keys_checked"] == 5          # 1e-12 < 1e-9 * 4
+    assert f["importance_small_max_abs_over_rowmax"] == pytest.approx(0.5e-12 / 4.0)
+    assert f["out_max_abs"] == pytest.approx(0.001)
+    # a keep mask that swaps the threshold token with a near tie
+    imp = np.array([[5.0, 4.0, 3.0, 3.0 * (1 - 1e-7), 1.0]], dtype=np.float32)
+    keep = np.array([[True, True, False, True, False]])
+    s = O.selection_figures(keep, imp, 3, tie_rtol=1e-5)
+    assert s["mask_mismatches"] == 2 and s["mismatches_near_ties"] == 2
+    s = O.selection_figures(np.array([[True, False, True, True, False]]), imp, 3, tie_rtol=1e-5)
+    assert s["mask_mismatches"] == 2 and s["mismatches_near_ties"] == 1
+
+
+def test_cpu_baseline_sample_and_flops():
+    # The timed CPU baseline (bench.py): a fixed sample, FLOPs counted with
+    # the GPU metric's formula, and the arithmetic of the oracle.
+    from oracle import cpu_baseline as C
+    plan = C.sample_plan(1, 4, 2, 512, 64, True, target_flops=4 * 64 * 2 * 512 * 300)
+    assert plan[0][:2] == (0, 0) and plan[0][2] % 256 == 0
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, 4, 512, 64, generator=g)
+    k = torch.randn(1, 2, 512, 64, generator=g)
+    v = torch.randn(1, 2, 512, 64, generator=g)
+    units = C.prepare(q, k, v, [(0, 0, 0)])
+    fl, _ = C.run(units, 512, True, 0.125, 0.0, 0, True)
+    keys = 512 * 513 // 2
+    assert fl == 2 * (4 * 64 * keys + 2 * 64 * keys)
