@@ -426,6 +426,39 @@ def timed_steps(step, steps, stream):
     return t0.elapsed_time(t1), {k_: v_ / steps for k_, v_ in stage_ms.items()}
 
 
+def scoring_overhead(dev):
+    """The north star's scoring-overhead target on one GPU: evict() time over
+    the time of the same attention kernel alone (the launch that score=False
+    runs), for the reference's own all-query benchmark shape (a10g32k) and
+    for c5 (every query scored, H2O).  CUDA events between the launches."""
+    from flash_evict.prefill import _evict_impl
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for name in ("a10g32k", "c5"):
+        w = WORKLOADS[name]
+        q, k, v = make_inputs(w, 3000, dev, on_device=True)
+        kw = dict(w["kw"])
+        recent = kw.pop("reserved_recent", 0)
+        pool = kw.pop("pool_kernel", 1)
+        kw["causal"] = w["causal"]
+
+        def step(marks=None):
+            return _evict_impl(q, k, v, w["budget"], 0, recent, pool, marks, kw)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize(dev)
+        total_ms, stage_ms = timed_steps(step, 10, stream)
+        f_attn, f_rep, _ = flops(w)
+        ms = total_ms / 10
+        out[name] = {"workload": w["desc"], "evict_ms": ms, "stage_ms": stage_ms,
+                     "overhead_vs_attention_only": ms / stage_ms["attention"], "target": 1.8,
+                     "value": (f_attn + f_rep) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s"}
+        del q, k, v
+        torch.cuda.empty_cache()
+    return out
+
+
 def sharded_section(args, world, rank, local, dev, barrier):
     """The partitioned configurations at this world size: c4 query-sharded
     (row-statistics exchange + one all_reduce of the FP32 scores) and c5
@@ -754,6 +787,7 @@ def run_ours(args, w):
     extra = next_rows(w, q, k, v, res, dev, stream) if (world == 1 and mode == "replica") else None
     del res, bufs, pieces
     parity = parity_check(w, q, k, v) if (world == 1 and mode == "replica" and not args.no_parity) else None
+    overhead = scoring_overhead(dev) if (world == 1 and args.workload == "c3" and not args.no_sharded) else None
     sharded = None
     if args.workload == "c3" and not args.no_sharded:
         del q, k, v
@@ -807,6 +841,8 @@ def run_ours(args, w):
         line["parity"] = parity
     if sharded:
         line["sharded"] = sharded
+    if overhead:
+        line["scoring_overhead"] = overhead
     if world == 1 and not args.no_cpu_baseline:
         qc, kc, vc = make_inputs(w, 1000, "cpu")
         fl, times, threads, desc = cpu_sample(w, qc, kc, vc, 3)

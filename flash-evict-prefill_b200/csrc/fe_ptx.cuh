@@ -313,15 +313,26 @@ __device__ __forceinline__ float exp2_poly(float x) {
 }
 
 // exp2 of a packed pair on the FMA pipe with FP32x2 arithmetic: the same
-// Cody-Waite split and degree-4 minimax coefficients as exp2_poly, but the
-// argument is clamped at -125 instead of selecting 0 below it, so arguments
-// of -125 and less (masked -inf included) give 2^-125 * p(0) ~ 2.4e-38
-// rather than 0.  Used where the result only enters sums and 16-bit P values,
-// for which that difference is far below their resolution.
+// Cody-Waite split and degree-4 minimax coefficients as exp2_poly.  The
+// argument is clamped at -125 (NaN-propagating), so arguments of -125 and
+// less (masked -inf included) give 2^-125 * p(0) ~ 2.35e-38 rather than 0 --
+// for sums and 16-bit P values that is far below their resolution.  2^n is
+// applied as a float multiply (its bits built from rint's low mantissa bits),
+// so a NaN argument gives NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t a2) {
   float a0, a1;
   f2_unpack(a2, a0, a1);
-  const uint64_t x2 = f2_pack(fmaxf(a0, -125.0f), fmaxf(a1, -125.0f));
+  const uint64_t x2 = f2_pack(fmax_nan(a0, -125.0f), fmax_nan(a1, -125.0f));
   const uint64_t t2 = f2_add(x2, f2_pack(12582912.0f, 12582912.0f));  // rint lands in the low mantissa bits
   const uint64_t n2 = f2_add(t2, f2_pack(-12582912.0f, -12582912.0f));
   const uint64_t f2 = f2_fma(n2, f2_pack(-1.0f, -1.0f), x2);  // f = x - rint(x), |f| <= 0.5
@@ -330,11 +341,12 @@ __device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t a2) {
   p2 = f2_fma(p2, f2, f2_pack(0.240247443318367f, 0.240247443318367f));
   p2 = f2_fma(p2, f2, f2_pack(0.6931217908859253f, 0.6931217908859253f));
   p2 = f2_fma(p2, f2, f2_pack(0.9999992847442627f, 0.9999992847442627f));
-  float p0, p1, t0, t1;
-  f2_unpack(p2, p0, p1);
+  float t0, t1;
   f2_unpack(t2, t0, t1);
-  return f2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
-                 __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
+  // 2^n = bits (n + 127) << 23; t's bits end in n, so (t << 23) + (127 << 23).
+  const uint64_t s2 = f2_pack(__int_as_float((__float_as_int(t0) << 23) + 0x3f800000),
+                              __int_as_float((__float_as_int(t1) << 23) + 0x3f800000));
+  return f2_mul(p2, s2);
 }
 
 // Pack two FP32 values into one 32-bit word of 16-bit elements, `lo` in the

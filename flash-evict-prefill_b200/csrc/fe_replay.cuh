@@ -14,10 +14,12 @@
 // The per-query normaliser and weight fold into one exponent bias:
 //   w_q / l_q * exp2(x - m_q) = exp2(x - bias_q),
 //   bias_q = m_q + log2(l_q) - decay*log2(e)*(q - (N-1))
-// with bias_q = +inf for rows outside the window or past N.  The reduction is
-// MUFU-bound, so 2 of every 16 exponentials run on the FMA pipe (exp2_poly,
-// relative error < 3e-6) and the exponent arithmetic uses packed FP32x2.  Query tiles whose
-// every weight is below 2^-127 (decay * distance beyond ~88) are skipped.
+// with bias_q = +inf for rows outside the window or past N.  The reduction
+// needs more exponentials than MUFU delivers per S^T MMA, so a share of them
+// (REPLAY_POLY_PAIRS column pairs of every 8) runs on the FMA pipe as a packed
+// FP32x2 polynomial (exp2_poly_x2, relative error < 3e-6), and the exponent
+// arithmetic uses packed FP32x2 too.  Query tiles whose every weight is below
+// 2^-127 (decay * distance beyond ~88) are skipped.
 //
 // Roles: REPLAY_WGS reduce warpgroups (thread = key) -- warpgroup w takes
 // items w, w+WGS, w+2*WGS, ...; item i's S^T lives in TMEM buffer i % NBUF
@@ -28,6 +30,8 @@
 // The warpgroups' FP64 sums of a key are added in a fixed order at the end
 // (deterministic).
 #pragma once
+
+#include <type_traits>
 
 #include "fe_ptx.cuh"
 
@@ -49,9 +53,13 @@ struct ReplayParams {
   uint64_t timeout_ns;
 };
 
-// Exponentials per 16 evaluated by exp2_poly (FMA pipe) instead of MUFU ex2;
-// the replay is MUFU-bound (16384 exponentials per 512-cycle S^T MMA).
-constexpr int REPLAY_POLY = 2;
+// Column pairs per 8 (off the diagonal tile) exponentiated by exp2_poly_x2
+// on the FMA pipe instead of MUFU ex2: the reduction needs 16384
+// exponentials per 512-cycle S^T MMA, more than MUFU delivers in that time.
+#ifndef FE_REPLAY_POLY_PAIRS
+#define FE_REPLAY_POLY_PAIRS 2
+#endif
+constexpr int REPLAY_POLY_PAIRS = FE_REPLAY_POLY_PAIRS;
 // Reduce warpgroups per CTA and S^T buffers per warpgroup; TMEM holds
 // 4 buffers per SM, so CTAs per SM = 4 / (WGS * SBUF).  Double-buffered S^T
 // (SBUF 2: WGS 2 with one CTA per SM, or WGS 1 with two) measured 10-25 %
@@ -314,7 +322,17 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     uint32_t li = 0;  // this warpgroup's item count
     bool ok = true;
     const uint64_t sc2 = f2_pack(sc, sc);
-    for (; it.valid(); it.advance(C::WGS), ++li) {
+    // One item: wait for its S^T, reduce it into `acc`, release the buffer.
+    // The diagonal tile (causal, query tile == key tile) is its own
+    // instantiation: columns q < key are masked to -inf and every
+    // exponential runs on MUFU, so masked entries are exactly 0.  Elsewhere
+    // REPLAY_POLY_PAIRS column pairs of every 8 are exponentiated on the FMA
+    // pipe (exp2_poly_x2, packed) and the rest on MUFU.  The diagonal items
+    // come first in a CTA's item order, so the two instantiations run as two
+    // loops one after the other, each with straight-line code per item
+    // (branching per 32-column quarter instead measured 7-8 % slower).
+    auto process_item = [&](auto diag_tag) -> bool {
+      constexpr bool DIAG = decltype(diag_tag)::value;
       const int bb = li & 1;
       const float* wbias = sbias + warp * 256 + bb * 128;
       // global item index wg + li*WGS -> S^T buffer and its use count
@@ -322,17 +340,14 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
       const int sb = static_cast<int>(gi % C::NBUF);
       const uint32_t tS = tS0 + sb * 128;
       __syncwarp();  // this item's bias is written; the other buffer is free
-      ok = warp_all(mbar_wait(&s_full[sb], (gi / C::NBUF) & 1, TO, abort_flag));
-      if (!ok) break;
+      if (!warp_all(mbar_wait(&s_full[sb], (gi / C::NBUF) & 1, TO, abort_flag))) return false;
       tc_fence_after();
-      const bool diag = p.causal && it.qt == kt;
       uint64_t acc2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
       // exp2(x*sc - bias_q) over the 128 query columns in four 32-column
-      // quarters: packed FP32x2 FMA for the exponents, REPLAY_POLY of every 16
-      // on the FMA pipe (exp2_poly) and the rest on MUFU, packed adds into four
-      // pair accumulators.  Diagonal tile: columns q < key are masked to -inf.
+      // quarters: packed FP32x2 FMA for the exponents, packed adds into four
+      // pair accumulators.
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         float x[32];
@@ -350,16 +365,23 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
           for (int hh = 0; hh < 2; ++hh) {
             const int c = c4 * 4 + hh * 2;
             const int col = h * 32 + c;
-            float a0, a1;
-            f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sc2, hh == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w)),
-                      a0, a1);
-            if (diag) {
+            const uint64_t a2 =
+                f2_fma(f2_pack(x[c], x[c + 1]), sc2, hh == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w));
+            uint64_t p2;
+            if constexpr (DIAG) {
+              float a0, a1;
+              f2_unpack(a2, a0, a1);
               a0 = (col >= kr) ? a0 : -INFINITY;
               a1 = (col + 1 >= kr) ? a1 : -INFINITY;
+              p2 = f2_pack(ex2_approx(a0), ex2_approx(a1));
+            } else if (((col & 15) >> 1) >= 8 - REPLAY_POLY_PAIRS) {
+              p2 = exp2_poly_x2(a2);
+            } else {
+              float a0, a1;
+              f2_unpack(a2, a0, a1);
+              p2 = f2_pack(ex2_approx(a0), ex2_approx(a1));
             }
-            const float p0 = ((col & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a0) : ex2_approx(a0);
-            const float p1 = (((col + 1) & 15) >= 16 - REPLAY_POLY) ? exp2_poly(a1) : ex2_approx(a1);
-            acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], f2_pack(p0, p1));
+            acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], p2);
           }
         }
         if (h == 1) {
@@ -378,7 +400,10 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
       f2_unpack(acc2[2], a4, a5);
       f2_unpack(acc2[3], a6, a7);
       acc += static_cast<double>(((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7)));
-    }
+      return true;
+    };
+    for (; it.valid() && p.causal && it.qt == kt && ok; it.advance(C::WGS), ++li) ok = process_item(std::true_type{});
+    for (; it.valid() && ok; it.advance(C::WGS), ++li) ok = process_item(std::false_type{});
     // Combine the four warpgroups' sums of each key in a fixed order.
     sred[wg * 128 + kr] = acc;
     named_bar_sync(1, C::WGS * 128);

@@ -20,8 +20,20 @@
  *  - `stream` is a cudaStream_t passed as void*; every launch is asynchronous
  *    on it and no entry point synchronizes the host.
  *  - Return value: FE_STATUS_OK or an error code; fe_last_error() gives the
- *    message for the calling thread.  Device-side watchdog timeouts surface
- *    through fe_device_status().
+ *    message for the calling thread.
+ *  - Errors of kernels that ran after their call returned: every device-side
+ *    wait is bounded (fe_set_watchdog_ns); a kernel that gives up records
+ *    FE_STATUS_TIMEOUT (a gather kernel records FE_STATUS_BAD_INDEX) in the
+ *    device status word and, once the library has attached it, in a word of
+ *    mapped pinned host memory for that device.  Every compute entry point
+ *    reads that host word on entry without synchronizing: a code found there
+ *    is returned as the call's error (the call launches nothing) and cleared.
+ *    The first compute call on a device in a CUDA context attaches the word
+ *    (one pinned host allocation per process, and a one-thread kernel on the
+ *    caller's stream); calls made while the stream is being captured do not
+ *    attach.  Outputs of a kernel that gave up hold NaN where it could mark
+ *    them (attention rows and their statistics, importance, SnapKV scores).
+ *    fe_device_status() is the synchronous check.
  *  - A "query block" is FE_QUERY_BLOCK consecutive query rows.  Passing
  *    query_blocks == NULL processes all rows; otherwise only the listed block
  *    indices (device int32 array) are processed, which is how a rank of a
@@ -217,7 +229,14 @@ FE_API int fe_snap_scores(const void* q, const int64_t* q_strides, const void* k
  *    (cudaGetSymbolAddress); make that first call before any stream capture.
  *  - All calls on a device share the one array: calls that can overlap on the
  *    GPU (different streams, no ordering between them) race on it.  Nothing
- *    in it has to start zeroed; each call writes what it later reads.
+ *    in it has to start zeroed: the attention kernel writes every row the
+ *    replay reads earlier on the same stream -- valid statistics, or NaN if
+ *    that kernel gave up on a wait (watchdog), so an aborted call yields NaN
+ *    importance, never the previous call's statistics.
+ *  - A timeout of an earlier call's kernel is returned as this call's error
+ *    when the host status word is attached; this entry point never attaches
+ *    it (that allocates pinned host memory), so make one call of another
+ *    entry point on the device first, or poll fe_device_status().
  *  - Calls no cudaMalloc, cudaFree or allocating library routine. */
 FE_API int fe_evict_noalloc(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                             const void* v, const int64_t* v_strides, void* out, float* importance,
@@ -228,7 +247,7 @@ FE_API int fe_evict_noalloc(const void* q, const int64_t* q_strides, const void*
 
 /* Read (and optionally clear) the device status word of `device`: the largest
  * FE_STATUS_* code any kernel raised since the last clear.  Synchronizes that
- * device. */
+ * device; clearing also clears the device's host status word. */
 FE_API int fe_device_status(int device, int clear, int* status_out);
 
 /* Watchdog limit for every device-side wait, in nanoseconds (default 2e9). */
@@ -236,12 +255,14 @@ FE_API void fe_set_watchdog_ns(int64_t ns);
 
 /* Launch a kernel whose bounded wait can never be satisfied, with the given
  * limit; it raises FE_STATUS_TIMEOUT and returns cleanly.  Used by tests to
- * exercise the timeout path without hanging a GPU. */
+ * exercise the timeout path without hanging a GPU.  Attaches the host status
+ * word of the current device (it does not report an earlier pending code). */
 FE_API int fe_watchdog_selftest(int64_t timeout_ns, void* stream);
 
 /* Evaluate the kernels' two exp2 implementations elementwise: out_poly = the
- * FMA-pipe polynomial (Cody-Waite reduction + degree-4 minimax, used for a
- * share of the softmax exponentials), out_mufu = the hardware ex2.approx.
+ * packed FP32x2 FMA-pipe polynomial (Cody-Waite reduction + degree-4 minimax,
+ * used for a share of the replay's exponentials; arguments below -125 give
+ * 2^-125 * p(0), about 2.35e-38), out_mufu = the hardware ex2.approx.
  * Diagnostic for tests; no counterpart in the reference (Triton's exp2). */
 FE_API int fe_selftest_exp2(const float* in, float* out_poly, float* out_mufu, int64_t n, void* stream);
 
