@@ -79,7 +79,10 @@ constexpr int FWD_POLY = 0;
 // FP32x2 on the FMA pipe) instead of MUFU ex2.  Measured at 2/3/4 pairs: the
 // attention kernel got 3 %/7 %/13 % slower (c3), so MUFU throughput is not
 // what bounds this softmax; kept at 0.
-constexpr int FWD_POLY_PAIRS = 0;
+#ifndef FE_FWD_POLY_PAIRS
+#define FE_FWD_POLY_PAIRS 0
+#endif
+constexpr int FWD_POLY_PAIRS = FE_FWD_POLY_PAIRS;
 // Lazy rescale threshold (log2 units): the max used for the exponentials only
 // moves when the row's true max exceeds it by more than this, so P <= 2^this.
 constexpr float FWD_RESCALE_LOG2 = 8.0f;
