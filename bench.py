@@ -467,7 +467,7 @@ def sharded_section(args, world, rank, local, dev, barrier):
     the same inputs on its own GPU.  Times are the maximum over ranks."""
     import torch.distributed as dist
     from flash_evict import evict
-    from flash_evict.distributed import evict_query_sharded, first_scored_row, head_unit_plan, query_block_plan
+    from flash_evict.distributed import evict_query_sharded, first_scored_row, head_blocks, query_block_plan
     from flash_evict.prefill import _evict_impl
 
     stream = torch.cuda.current_stream(dev)
@@ -489,7 +489,7 @@ def sharded_section(args, world, rank, local, dev, barrier):
         kw["causal"] = w["causal"]
         g = w["hq"] // w["hkv"]
         mode = "query" if name == "c4" else "heads"
-        runs = head_unit_plan(w["b"], w["hkv"], world)[rank]
+        runs = head_blocks(w["b"], w["hkv"], world)[rank]
 
         def step(marks=None):
             if world == 1:
@@ -497,8 +497,8 @@ def sharded_section(args, world, rank, local, dev, barrier):
             if mode == "query":
                 return evict_query_sharded(q, k, v, budget, reserved_recent=recent, pool_kernel=pool, _marks=marks,
                                            **kw)
-            return [_evict_impl(q[b:b + 1, h0 * g:h1 * g], k[b:b + 1, h0:h1], v[b:b + 1, h0:h1], budget, 0, recent,
-                                pool, marks, kw) for b, h0, h1 in runs]
+            return [_evict_impl(q[b0:b1, h0 * g:h1 * g], k[b0:b1, h0:h1], v[b0:b1, h0:h1], budget, 0, recent,
+                                pool, marks, kw) for b0, b1, h0, h1 in runs]
 
         steps = max(3, min(args.steps, 10 if name == "c4" else 20))
         for _ in range(3):
@@ -522,10 +522,10 @@ def sharded_section(args, world, rank, local, dev, barrier):
                 lo, hi = blk * 256, min(w["n"], (blk + 1) * 256)
                 ok &= torch.equal(out[:, :, lo:hi], ref[0][:, :, lo:hi])
         elif world > 1:
-            for (b, h0, h1), (out, imp, idx, mask) in zip(runs, mine):
-                ok &= torch.equal(out, ref[0][b:b + 1, h0 * g:h1 * g])
-                ok &= torch.equal(imp.view(torch.int32), ref[1][b:b + 1, h0:h1].view(torch.int32))
-                ok &= torch.equal(idx, ref[2][b:b + 1, h0:h1]) and torch.equal(mask, ref[3][b:b + 1, h0:h1])
+            for (b0, b1, h0, h1), (out, imp, idx, mask) in zip(runs, mine):
+                ok &= torch.equal(out, ref[0][b0:b1, h0 * g:h1 * g])
+                ok &= torch.equal(imp.view(torch.int32), ref[1][b0:b1, h0:h1].view(torch.int32))
+                ok &= torch.equal(idx, ref[2][b0:b1, h0:h1]) and torch.equal(mask, ref[3][b0:b1, h0:h1])
         else:
             for a_, b_ in zip(mine, ref):
                 ok &= torch.equal(a_.view(torch.int32) if a_.dtype == torch.float32 else a_,
@@ -543,8 +543,9 @@ def sharded_section(args, world, rank, local, dev, barrier):
                          f"by key tiles after the statistics exchange of rows >= {r0}")
         else:
             nccl = {}
-            plan_note = (f"{w['b'] * w['hkv']} (batch, kv-head) units in contiguous ranges "
-                         f"({len(runs)} run(s) on rank 0)") if world > 1 else "single GPU, plain evict()"
+            plan_note = ((f"{w['b'] * w['hkv']} (batch, kv-head) units in contiguous ranges "
+                          f"({len(runs)} evict() call(s) on rank 0: whole batches merged)") if world > 1
+                         else "single GPU, plain evict()")
         del q, k, v, ref, mine
         torch.cuda.empty_cache()
         result[name] = {
@@ -560,7 +561,7 @@ def sharded_section(args, world, rank, local, dev, barrier):
 def run_ours(args, w):
     import torch.distributed as dist
     from flash_evict import _lib, evict
-    from flash_evict.distributed import evict_query_sharded, head_unit_plan
+    from flash_evict.distributed import evict_query_sharded, head_blocks
     from flash_evict.prefill import _evict_impl
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -582,7 +583,7 @@ def run_ours(args, w):
     f_attn, f_rep, f_rep_all = flops(w)
     stream = torch.cuda.current_stream(dev)
     g = w["hq"] // w["hkv"]
-    runs = head_unit_plan(w["b"], w["hkv"], world)[rank] if mode == "heads" else None
+    runs = head_blocks(w["b"], w["hkv"], world)[rank] if mode == "heads" else None
 
     # One step through the public API (flash_evict.evict, or the sharded
     # entry points); with `marks` the same body with CUDA events between the
@@ -598,7 +599,7 @@ def run_ours(args, w):
         if mode == "query":
             return evict_query_sharded(qq, kk, vv, budget, reserved_recent=recent, pool_kernel=pool, _marks=marks,
                                        **kw)
-        return [one(qq[b:b + 1, h0 * g:h1 * g], kk[b:b + 1, h0:h1], vv[b:b + 1, h0:h1], marks) for b, h0, h1 in runs]
+        return [one(qq[b0:b1, h0 * g:h1 * g], kk[b0:b1, h0:h1], vv[b0:b1, h0:h1], marks) for b0, b1, h0, h1 in runs]
 
     def barrier():
         if world > 1:
@@ -722,9 +723,9 @@ def run_ours(args, w):
     def pieces_of(dq, dk, dv):
         if mode == "heads":
             out_ = []
-            for b, h0, h1 in runs:
-                out_ += [(dq[b:b + 1, h0 * g:h1 * g], hq_[b:b + 1, h0 * g:h1 * g]),
-                         (dk[b:b + 1, h0:h1], hk_[b:b + 1, h0:h1]), (dv[b:b + 1, h0:h1], hv_[b:b + 1, h0:h1])]
+            for b0, b1, h0, h1 in runs:
+                out_ += [(dq[b0:b1, h0 * g:h1 * g], hq_[b0:b1, h0 * g:h1 * g]),
+                         (dk[b0:b1, h0:h1], hk_[b0:b1, h0:h1]), (dv[b0:b1, h0:h1], hv_[b0:b1, h0:h1])]
             return out_
         return [(dq, hq_), (dk, hk_), (dv, hv_)]
 

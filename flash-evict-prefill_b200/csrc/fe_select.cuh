@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
   __shared__ uint32_t hist[2][256];
   __shared__ uint32_t tot[256];
   __shared__ int warp_sums[72];
-  __shared__ uint32_t sel_digit, sel_krem;
+  __shared__ uint32_t sel_digit, sel_krem, sel_done;
   __shared__ long long counts[2];  // this CTA's {greater, equal} counts
 
   const int64_t N = p.N;
@@ -193,6 +193,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     // ---- radix select of the kk-th largest key over the whole cluster ----
     uint32_t prefix = 0, pmask = 0;
     uint32_t krem = static_cast<uint32_t>(kk);
+    if (threadIdx.x == 0) sel_done = 0u;
     for (int pass = 0; pass < 4; ++pass) {
       const int buf = pass & 1;
       const int shift = 24 - 8 * pass;
@@ -242,6 +243,8 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
             if (cum + c >= krem) {
               sel_digit = static_cast<uint32_t>(digit);
               sel_krem = krem - cum;
+              // Every key of this bucket is kept: the threshold can stop here.
+              sel_done = (cum + c == krem) ? 1u : 0u;
               break;
             }
             cum += c;
@@ -252,9 +255,16 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       prefix |= sel_digit << shift;
       pmask |= 255u << shift;
       krem = sel_krem;
+      const bool done = sel_done != 0u;
       __syncthreads();
+      if (done) {
+        // The bucket holding the kk-th largest key is kept whole: every key
+        // at or above its smallest possible value (prefix, low bits zero).
+        krem = 0xFFFFFFFFu;
+        break;
+      }
     }
-    const uint32_t T = prefix;    // the kk-th largest key
+    const uint32_t T = prefix;    // the kk-th largest key, or the kept bucket's floor
     const uint32_t need_eq = krem; // how many keys equal to T are kept (lowest indices)
 
     // ---- per-CTA counts, exchanged for offsets ----
@@ -288,16 +298,36 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       }
     }
     cluster.sync();
-    long long gt_before = 0, eq_before = 0;
-    for (int rr = 0; rr < crank; ++rr) {
+    long long gt_before = 0, eq_before = 0, eq_total = 0;
+    for (int rr = 0; rr < C; ++rr) {
       const long long* rc = cluster.map_shared_rank(&counts[0], rr);
-      gt_before += rc[0];
-      eq_before += rc[1];
+      if (rr < crank) {
+        gt_before += rc[0];
+        eq_before += rc[1];
+      }
+      eq_total += rc[1];
     }
     // Keep remote CTAs' shared memory alive until everyone has read it.
     cluster.sync();
 
     // ---- ordered compaction ----
+    if (eq_total <= static_cast<long long>(need_eq)) {
+      // Every key equal to T is kept (the usual case: no tie is cut at the
+      // threshold), so kept == (k >= T) and one scan per tile places it.
+      long long run = gt_before + eq_before;
+      for (int base = 0; base < len; base += SEL_THREADS) {
+        const int i = base + threadIdx.x;
+        const bool in = i < len;
+        const bool kept = in && key_at(i) >= T;
+        int tot_kept;
+        const int pos = block_flag_scan(kept, warp_sums, &tot_kept);
+        if (in) {
+          if (kept) out_idx[run + pos] = lo + i;
+          out_mask[lo + i] = kept ? keep_v : evict_v;
+        }
+        run += tot_kept;
+      }
+    } else {
     long long run_gt = gt_before, run_eq = eq_before;
     for (int base = 0; base < len; base += SEL_THREADS) {
       const int i = base + threadIdx.x;
@@ -320,6 +350,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       const long long kept_eq_after = min(run_eq + tot_eq, static_cast<long long>(need_eq));
       run_gt += tot_kept - (kept_eq_after - kept_eq_before);
       run_eq += tot_eq;
+    }
     }
   }
 

@@ -31,8 +31,8 @@ from . import _lib
 from .prefill import (_attention, _check_prefill_args, _check_select_args, _replay, _select, _tma_view,
                       _validate)
 
-__all__ = ["query_block_plan", "head_unit_plan", "key_tile_plan", "first_scored_row", "evict_query_sharded",
-           "evict_head_sharded"]
+__all__ = ["query_block_plan", "head_unit_plan", "head_blocks", "key_tile_plan", "first_scored_row",
+           "evict_query_sharded", "evict_head_sharded"]
 
 BLOCK = _lib.QUERY_BLOCK
 
@@ -102,6 +102,24 @@ def head_unit_plan(batch, kv_heads, world):
     return plan
 
 
+def head_blocks(batch, kv_heads, world):
+    """head_unit_plan with consecutive whole batches merged: per rank a list
+    of (b0, b1, h0, h1) blocks -- batches b0..b1-1, kv heads h0..h1-1 -- so a
+    rank whose range spans whole batches runs them as one evict() call (three
+    launches) instead of one call per batch."""
+    out = []
+    for runs in head_unit_plan(batch, kv_heads, world):
+        blocks = []
+        for b, h0, h1 in runs:
+            whole = h0 == 0 and h1 == kv_heads
+            if whole and blocks and blocks[-1][2] == 0 and blocks[-1][3] == kv_heads and blocks[-1][1] == b:
+                blocks[-1] = (blocks[-1][0], b + 1, 0, kv_heads)
+            else:
+                blocks.append((b, b + 1, h0, h1))
+        out.append(blocks)
+    return out
+
+
 def _world(group):
     if group is None and not dist.is_initialized():
         return 0, 1
@@ -113,17 +131,18 @@ def evict_head_sharded(q, k, v, budget, *, group=None, recent=0, reserved_recent
     """Run evict() on this rank's (batch, kv-head) units; no communication.
 
     q/k/v are the full [B, H, N, D] tensors (views are taken, nothing is
-    copied).  Returns a list of (b, h0, h1, out, importance, indices, mask)
-    for the runs this rank owns; `out` covers query heads h0*G..h1*G-1.
+    copied).  Returns a list of (b0, b1, h0, h1, out, importance, indices,
+    mask) for the blocks this rank owns (head_blocks): batches b0..b1-1 and kv
+    heads h0..h1-1; `out` covers query heads h0*G..h1*G-1 of those batches.
     """
     from .prefill import evict
     rank, world = _world(group)
     g = q.shape[1] // k.shape[1]
     results = []
-    for b, h0, h1 in head_unit_plan(q.shape[0], k.shape[1], world)[rank]:
-        res = evict(q[b:b + 1, h0 * g:h1 * g], k[b:b + 1, h0:h1], v[b:b + 1, h0:h1], budget, recent=recent,
+    for b0, b1, h0, h1 in head_blocks(q.shape[0], k.shape[1], world)[rank]:
+        res = evict(q[b0:b1, h0 * g:h1 * g], k[b0:b1, h0:h1], v[b0:b1, h0:h1], budget, recent=recent,
                     reserved_recent=reserved_recent, pool_kernel=pool_kernel, **prefill_kwargs)
-        results.append((b, h0, h1) + tuple(res))
+        results.append((b0, b1, h0, h1) + tuple(res))
     return results
 
 

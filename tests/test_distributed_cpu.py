@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from flash_evict.distributed import (BLOCK, _block_cost, _query_sharded, first_scored_row, head_unit_plan,
+from flash_evict.distributed import (BLOCK, _block_cost, _query_sharded, first_scored_row, head_blocks, head_unit_plan,
                                      key_tile_plan, query_block_plan)
 from oracle import restate as O
 
@@ -53,6 +53,21 @@ def test_head_unit_plan_covers_units(batch, heads, world):
     assert sorted(units) == [(b, h) for b in range(batch) for h in range(heads)]
     sizes = [sum(h1 - h0 for _, h0, h1 in runs) for runs in plan]
     assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("batch,heads,world", [(8, 32, 8), (8, 32, 2), (8, 32, 3), (1, 8, 8), (2, 3, 4), (5, 4, 2)])
+def test_head_blocks_merge_whole_batches(batch, heads, world):
+    blocks = head_blocks(batch, heads, world)
+    units = [(b, h) for bl in blocks for (b0, b1, h0, h1) in bl for b in range(b0, b1) for h in range(h0, h1)]
+    assert sorted(units) == [(b, h) for b in range(batch) for h in range(heads)]
+    for bl in blocks:
+        for b0, b1, h0, h1 in bl:
+            assert b1 > b0 and h1 > h0
+            assert b1 - b0 == 1 or (h0 == 0 and h1 == heads)   # several batches only when whole
+        whole = [x for x in bl if x[2] == 0 and x[3] == heads]
+        assert all(a[1] != c[0] for a, c in zip(whole, whole[1:]))  # no two adjacent whole blocks left unmerged
+    if world == 2 and batch == 8:
+        assert blocks == [[(0, 4, 0, heads)], [(4, 8, 0, heads)]]
 
 
 def _oracle_attend(q, k, v, blocks, causal, scale):

@@ -46,9 +46,9 @@ def _worker(rank, world, port, out_dir):
         runs = evict_head_sharded(qb, kb, vb, 256, causal=False, value_weighted=False)
         refb = evict(qb, kb, vb, 256, causal=False, value_weighted=False)
         head_ok = True
-        for b, h0, h1, o, i, ix, m in runs:
-            head_ok &= torch.equal(o, refb[0][b:b + 1, h0:h1]) and torch.equal(i, refb[1][b:b + 1, h0:h1])
-            head_ok &= torch.equal(ix, refb[2][b:b + 1, h0:h1]) and torch.equal(m, refb[3][b:b + 1, h0:h1])
+        for b0, b1, h0, h1, o, i, ix, m in runs:
+            head_ok &= torch.equal(o, refb[0][b0:b1, h0:h1]) and torch.equal(i, refb[1][b0:b1, h0:h1])
+            head_ok &= torch.equal(ix, refb[2][b0:b1, h0:h1]) and torch.equal(m, refb[3][b0:b1, h0:h1])
         torch.cuda.synchronize()
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), out_equal=torch.equal(out, ref[0]),
                  imp_equal=torch.equal(imp, ref[1]),
