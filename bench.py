@@ -731,8 +731,15 @@ def run_ours(args, w):
 
     pieces = [pieces_of(*bf) for bf in bufs]
     h2d = sum(src.numel() * src.element_size() for _, src in pieces[0])
-    h2d_stream = torch.cuda.Stream(dev)
-    d2h_stream = torch.cuda.Stream(dev)
+    # Two copy schedules: "duplex" copies in and out on separate streams (the
+    # two PCIe directions overlap each other and the compute); "serial" puts
+    # both on one copy stream (they still overlap the compute).  Hosts differ:
+    # on some, concurrent H2D and D2H collapse to a fraction of either alone,
+    # so a short untimed probe of both picks the faster (the same on all ranks).
+    copy_in = torch.cuda.Stream(dev)
+    copy_out = torch.cuda.Stream(dev)
+    schedules = {"duplex": (copy_in, copy_out), "serial": (copy_in, copy_in)}
+    h2d_stream, d2h_stream = schedules["duplex"]
     host_out = None
     d2h = 0
 
@@ -773,7 +780,21 @@ def run_ours(args, w):
         return res_
 
     e2e_steps = max(2, min(args.steps, 50))
-    e2e_run(2)  # warm-up of the pipelined loop
+    probe = {}
+    for name_, (si, so) in schedules.items():
+        h2d_stream, d2h_stream = si, so
+        e2e_run(2)  # warm-up of the pipelined loop
+        torch.cuda.synchronize(dev)
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(h2d_stream)
+        e2e_run(4)
+        p1.record(d2h_stream)
+        torch.cuda.synchronize(dev)
+        probe[name_] = max_over_ranks(p0.elapsed_time(p1)) / 4
+    schedule = min(probe, key=probe.get)
+    h2d_stream, d2h_stream = schedules[schedule]
+    e2e_run(2)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -827,10 +848,12 @@ def run_ours(args, w):
                      "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a multi-second loop)"},
         "clocks": clk,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms,
+                "ms_per_step": e2e_ms, "copy_schedule": schedule,
+                "copy_schedule_probe_ms_per_step": probe,
                 "how": "per step: H2D of q/k/v from pinned host memory, evict(), D2H of every returned tensor "
-                       "(out, importance, indices, mask) to pinned host memory; copies on their own streams, "
-                       "double-buffered, overlapping the neighbouring steps' compute"},
+                       "(out, importance, indices, mask) to pinned host memory; copies on their own stream(s), "
+                       "double-buffered, overlapping the neighbouring steps' compute; the faster of the duplex "
+                       "and serial copy schedules in an untimed probe"},
         "gpu_launches": launches_per_step * args.steps,
         "device_status": status,
     }

@@ -345,26 +345,23 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
       uint64_t acc2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc2[c] = 0ull;
-      // exp2(x*sc - bias_q) over the 128 query columns in four 32-column
-      // quarters: packed FP32x2 FMA for the exponents, packed adds into four
-      // pair accumulators.
+      // exp2(x*sc - bias_q) over the 128 query columns in eight 16-column
+      // chunks, the next chunk's TMEM load in flight while this one is
+      // reduced: packed FP32x2 FMA for the exponents, packed adds into four
+      // pair accumulators (the same order as one pass over the columns).
+      float xa[16], xb[16];
+      tmem_ld16_nowait(tS, reinterpret_cast<uint32_t*>(xa));
+      tmem_wait_ld16(reinterpret_cast<uint32_t*>(xa));
+      auto chunk = [&](const int h, float (&x)[16], float (&xn)[16]) {
+        if (h < 7) tmem_ld16_nowait(tS + (h + 1) * 16, reinterpret_cast<uint32_t*>(xn));
+        const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 16);
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float x[32];
-        tmem_ld32_sync(tS + h * 32, reinterpret_cast<uint32_t*>(x));
-        if (h == 3) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[sb]);
-        }
-        const float4* nb4 = reinterpret_cast<const float4*>(wbias + h * 32);
-#pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
+        for (int c4 = 0; c4 < 4; ++c4) {
           const float4 nb = nb4[c4];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const int c = c4 * 4 + hh * 2;
-            const int col = h * 32 + c;
+            const int col = h * 16 + c;
             const uint64_t a2 =
                 f2_fma(f2_pack(x[c], x[c + 1]), sc2, hh == 0 ? f2_pack(nb.x, nb.y) : f2_pack(nb.z, nb.w));
             uint64_t p2;
@@ -381,10 +378,17 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
               f2_unpack(a2, a0, a1);
               p2 = f2_pack(ex2_approx(a0), ex2_approx(a1));
             }
-            acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], p2);
+            acc2[(col >> 1) & 3] = f2_add(acc2[(col >> 1) & 3], p2);
           }
         }
-        if (h == 1) {
+        if (h < 7) tmem_wait_ld16(reinterpret_cast<uint32_t*>(xn));
+        if (h == 6) {
+          // every load of this S^T buffer has completed: release it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[sb]);
+        }
+        if (h == 3) {
           ReplayItems nx = it;
           nx.advance(C::WGS);
           if (nx.valid()) {
@@ -393,6 +397,11 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
             if (nx.valid()) load_stats(nx, ml_next);
           }
         }
+      };
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        if (h & 1) chunk(h, xb, xa);
+        else chunk(h, xa, xb);
       }
       float a0, a1, a2, a3, a4, a5, a6, a7;
       f2_unpack(acc2[0], a0, a1);
