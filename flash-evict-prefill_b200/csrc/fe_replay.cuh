@@ -428,13 +428,36 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
       if (p.weighted) {
         using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
         const T* vrow = reinterpret_cast<const T*>(p.v) + b * p.v_sb + hkv * p.v_sh + static_cast<int64_t>(key) * p.v_sn;
+        // ||v_key||_1 in channel order.  The row is read with 16-byte loads
+        // issued back to back (a scalar loop of dependent 2-byte loads ran
+        // at memory latency per channel and dominated short replays); the
+        // adds keep the sequential channel order.
+        auto to_f = [](T h) -> float {
+          if constexpr (BF16) return __bfloat162float(h);
+          else return __half2float(h);
+        };
         float s = 0.f;
-        for (int d = 0; d < p.D; ++d) {
-          float x;
-          if constexpr (BF16) x = __bfloat162float(vrow[d]);
-          else x = __half2float(vrow[d]);
-          s += fabsf(x);
+        int d = 0;
+        if ((reinterpret_cast<uintptr_t>(vrow) & 15u) == 0) {
+          constexpr int NV = DP / 8;  // 16-byte chunks; four in flight at a time
+#pragma unroll
+          for (int i0 = 0; i0 < NV; i0 += 4) {
+            uint4 u[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if ((i0 + i) * 8 + 8 <= p.D) u[i] = __ldg(reinterpret_cast<const uint4*>(vrow) + i0 + i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if ((i0 + i) * 8 + 8 <= p.D) {
+                const T* h = reinterpret_cast<const T*>(&u[i]);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s += fabsf(to_f(h[e]));
+              }
+            }
+          }
+          d = p.D & ~7;
         }
+        for (; d < p.D; ++d) s += fabsf(to_f(vrow[d]));
         vn = s;
       }
       p.importance[(static_cast<size_t>(b) * p.Hkv + hkv) * p.N + key] = static_cast<float>(total) * vn;
