@@ -2,8 +2,10 @@
 //
 // Host side only: argument checks, TMA tensor-map encoding for arbitrarily
 // strided Q/K/V, kernel selection by head dimension and dtype, launches on the
-// caller's stream.  No allocation and no host synchronization on the compute
-// entry points.  The library links the CUDA runtime statically; because the
+// caller's stream.  No device allocation and no host synchronization on the
+// compute entry points; the first compute call of the process allocates one
+// small array of mapped pinned host memory for the per-device status words
+// (see attach_status).  The library links the CUDA runtime statically; because the
 // caller (PyTorch) has its own runtime instance, every entry point first makes
 // the device that owns the input pointer current for this runtime.
 #include <cuda.h>
