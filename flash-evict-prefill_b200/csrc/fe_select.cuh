@@ -185,7 +185,13 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       else return key_from_scores(i);
     };
     if constexpr (SMEM_KEYS) {
-      for (int i = threadIdx.x; i < len; i += SEL_THREADS) keys[i] = key_from_scores(i);
+      if (!pooled) {
+        // Four loads in flight per thread (the key pass is latency-bound).
+#pragma unroll 4
+        for (int i = threadIdx.x; i < len; i += SEL_THREADS) keys[i] = order_key(imp[lo + i]);
+      } else {
+        for (int i = threadIdx.x; i < len; i += SEL_THREADS) keys[i] = key_from_scores(i);
+      }
     }
     for (int i = threadIdx.x; i < 512; i += SEL_THREADS) (&hist[0][0])[i] = 0;
     __syncthreads();
