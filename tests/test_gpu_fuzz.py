@@ -13,12 +13,22 @@ import numpy as np
 import pytest
 import torch
 
-from common import selection_mismatch
+from common import record_figures, selection_mismatch
 from flash_evict import evict_compact
 from flash_evict.baselines import snap_scores
 from oracle import restate as O
 
 pytestmark = pytest.mark.gpu
+
+
+_WORST = {}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _record_worst():
+    yield
+    if _WORST:
+        record_figures("fuzz (48 random configurations, worst case)", dict(_WORST))
 
 
 def draw(seed):
@@ -58,6 +68,18 @@ def test_random_configuration(seed):
     np.testing.assert_allclose(out.float().cpu().numpy(), ref_out, atol=tol * max(1.0, c["qscale"]), rtol=0.006,
                                err_msg=str(c))
     np.testing.assert_allclose(imp.cpu().numpy(), ref_imp, atol=3e-3, rtol=3e-4, err_msg=str(c))
+    # The stated importance tolerance against the float64 oracle (same FP32
+    # scale as the reference): relative over keys holding at least 1e-6 of
+    # their row's largest importance, absolute (over the row maximum) below.
+    # Worst case measured over the 48 configurations on B200: 3.3e-6.
+    _, imp64 = O.materialized(qn, kn, vn, causal=c["causal"], recency_decay=c["decay"],
+                              observation_window=c["window"], value_weighted=c["weighted"],
+                              scale=float(np.float32(d ** -0.5)), dtype=np.float64)
+    figs = O.parity_figures(np.zeros(0), np.zeros(0), imp.cpu().numpy(), imp64)
+    _WORST["importance_max_rel"] = max(_WORST.get("importance_max_rel", 0.0), figs["importance_max_rel"])
+    assert figs["importance_max_rel"] < 1e-5, (c, figs)
+    assert figs["importance_small_max_abs_over_rowmax"] < 1e-6, (c, figs)
+    assert figs["importance_nonfinite"] == 0
     _, ref_keep = O.select_tokens(ref_imp, budget, reserved_recent=recent, pool_kernel=c["pool"])
     mism, ok = selection_mismatch(~mask.cpu().numpy(), ref_keep, imp.cpu().numpy(), ref_imp, 3e-3, 3e-4)
     assert ok, (c, mism)
