@@ -36,6 +36,8 @@
 // arithmetic, and double-buffered 64-key S tiles.
 #pragma once
 
+#include <type_traits>
+
 #include "fe_ptx.cuh"
 
 namespace fe {
@@ -142,6 +144,51 @@ __device__ __forceinline__ float row_max_scaled(const float (&x)[128], float sce
 #pragma unroll
   for (int c = 8; c < 128; c += 2) mm[(c >> 1) & 7] = fmax3(mm[(c >> 1) & 7], x[c], x[c + 1]);
   return fmax3(fmax3(mm[0], mm[1], mm[2]), fmax3(mm[3], mm[4], mm[5]), fmaxf(mm[6], mm[7])) * sce;
+}
+
+// One KV tile of a query row's softmax, with S already in registers: scale
+// and mask (GENERAL only: columns past `lim` get -inf), row max, lazy O
+// rescale, exponentials, row sum and the P store over the first 64 columns of
+// the S tile.
+template <bool BF16, int DV, bool GENERAL>
+__device__ __forceinline__ void fwd_softmax_tile(float (&x)[128], int j, int lim, float sc, float sce, bool sc_pos,
+                                                 float& m_used, float& l, uint32_t tS, uint32_t tO) {
+  if constexpr (GENERAL) {
+    if (!sc_pos) {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) x[c] *= sc;
+    }
+#pragma unroll
+    for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
+  }
+  // Row max first.  The max used for the exponentials only moves when the
+  // true max exceeds it by more than 2^8 (lazy rescale); tracking the max
+  // inside the exponential pass instead was measured slower (extreme logits
+  // force frequent redo passes).
+  const float m_new = fmaxf(m_used, row_max_scaled(x, sce));
+  if (j == 0) {
+    m_used = m_new;
+  } else if (__any_sync(0xffffffffu, m_new > m_used + FWD_RESCALE_LOG2)) {
+    // Rescale this warp's O rows; PV_t(j-1) is complete (see the header).
+    const float f = ex2_approx(m_used - m_new);
+    l *= f;
+    m_used = m_new;
+#pragma unroll 1
+    for (int c0 = 0; c0 < DV; c0 += 32) {
+      uint32_t o[32];
+      tmem_ld32_sync(tO + c0, o);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+      tmem_st32(tO + c0, o);
+    }
+    tmem_wait_st();
+  }
+  uint32_t pk[64];
+  float amax;
+  l += softmax_exp_pass<BF16, FWD_POLY, false, FWD_POLY_PAIRS>(x, sce, m_used, pk, amax);
+  tmem_st32(tS, pk);
+  tmem_st32(tS + 32, pk + 32);
+  tmem_wait_st();
 }
 
 template <bool BF16, int DQK, int DV>
@@ -381,9 +428,15 @@ __global__ void __launch_bounds__(384, 1)
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      ok = warp_all(mbar_wait(&s_full[t], j & 1, TO, abort_flag));
-      if (!ok) break;
+    // KV tiles that need per-element work (the diagonal tiles of a causal
+    // block, the ragged end of N; every tile for a non-positive scale) come
+    // last and run in a loop of their own, so the loop over all other tiles
+    // carries no masking code.
+    int n_plain = p.causal ? min(nt, rbase / 128) : nt;
+    if ((p.N % 128) != 0 && n_plain == nkv) n_plain = nkv - 1;
+    if (!sc_pos) n_plain = 0;
+    auto tile_step = [&](int j, auto general) -> bool {
+      if (!warp_all(mbar_wait(&s_full[t], j & 1, TO, abort_flag))) return false;
       tc_fence_after();
       float x[128];
       {
@@ -391,50 +444,15 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld64_sync(tS, xr);
         tmem_ld64_sync(tS + 64, xr + 64);
       }
-      const int kbase = j * 128;
-      const bool masked = (kbase + 128 > p.N) || (p.causal && kbase + 127 > rbase);
-      if (!sc_pos) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] *= sc;
-      }
-      if (masked) {
-        const int lim = (p.causal ? min(p.N - 1, row) : (p.N - 1)) - kbase;
-#pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = (c <= lim) ? x[c] : -INFINITY;
-      }
-      // Row max first.  The max used for the exponentials only moves when the
-      // true max exceeds it by more than 2^8 (lazy rescale); tracking the max
-      // inside the exponential pass instead was measured slower (extreme
-      // logits force frequent redo passes).
-      const float m_new = fmaxf(m_used, row_max_scaled(x, sce));
-      if (j == 0) {
-        m_used = m_new;
-      } else if (__any_sync(0xffffffffu, m_new > m_used + FWD_RESCALE_LOG2)) {
-        // Rescale this warp's O rows; PV_t(j-1) is complete (see header).
-        const float f = ex2_approx(m_used - m_new);
-        l *= f;
-        m_used = m_new;
-#pragma unroll 1
-        for (int c0 = 0; c0 < DV; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32_sync(tO + c0, o);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
-          tmem_st32(tO + c0, o);
-        }
-        tmem_wait_st();
-      }
-      uint32_t pk[64];
-      float amax;
-      const float tile_sum = softmax_exp_pass<BF16, FWD_POLY, false, FWD_POLY_PAIRS>(x, sce, m_used, pk, amax);
-      l += tile_sum;
-      tmem_st32(tS, pk);
-      tmem_st32(tS + 32, pk + 32);
-      tmem_wait_st();
+      const int lim = (p.causal ? min(p.N - 1, row) : (p.N - 1)) - j * 128;
+      fwd_softmax_tile<BF16, DV, decltype(general)::value>(x, j, lim, sc, sce, sc_pos, m_used, l, tS, tO);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
-    }
+      return true;
+    };
+    for (int j = 0; j < n_plain && ok; ++j) ok = tile_step(j, std::false_type{});
+    for (int j = n_plain; j < nt && ok; ++j) ok = tile_step(j, std::true_type{});
     if (nt > 0 && ok) ok = warp_all(mbar_wait(&o_full[t], 0, TO, abort_flag));
     if (nt > 0 && !ok && row < p.N) {
       // Aborted (watchdog): mark this row's statistics and output channels
