@@ -288,10 +288,14 @@ __global__ void __launch_bounds__(384, 1)
       tma_prefetch_desc(&tv);
       uint32_t loads[C::STAGES];
       for (int s = 0; s < C::STAGES; ++s) loads[s] = 0;
+      // Q is read once; K/V are re-read by every query block of the head
+      // group: keep them in L2 ahead of the streaming Q reads and O writes.
+      const uint64_t pol_q = l2_policy_evict_first();
+      const uint64_t pol_kv = l2_policy_evict_last();
       mbar_expect_tx(q_full, ((n0 > 0) + (n1 > 0)) * C::TILE);
       for (int c = 0; c < C::NCH; ++c) {
-        if (n0 > 0) tma_load_4d(smem + C::OFF_Q + c * 16384, &tq, q_full, c * 64, row0, hq, b);
-        if (n1 > 0) tma_load_4d(smem + C::OFF_Q + C::TILE + c * 16384, &tq, q_full, c * 64, row1, hq, b);
+        if (n0 > 0) tma_load_4d_hint(smem + C::OFF_Q + c * 16384, &tq, q_full, c * 64, row0, hq, b, pol_q);
+        if (n1 > 0) tma_load_4d_hint(smem + C::OFF_Q + C::TILE + c * 16384, &tq, q_full, c * 64, row1, hq, b, pol_q);
       }
       bool ok = true;
       for (int j = 0; j < nmax && ok; ++j) {
@@ -301,7 +305,8 @@ __global__ void __launch_bounds__(384, 1)
         if (!ok) break;
         mbar_expect_tx(&k_full[s], C::TILE);
         for (int c = 0; c < C::NCH; ++c)
-          tma_load_4d(smem + C::OFF_K + s * C::TILE + c * 16384, &tk, &k_full[s], c * 64, j * 128, hkv, b);
+          tma_load_4d_hint(smem + C::OFF_K + s * C::TILE + c * 16384, &tk, &k_full[s], c * 64, j * 128, hkv, b,
+                           pol_kv);
         if (use > 0) ok = mbar_wait(&v_empty[s], (use - 1) & 1, TO, abort_flag);
         if (!ok) {
           loads[s] = use * 2 + 1;  // K of this use in flight, V not issued
@@ -309,8 +314,8 @@ __global__ void __launch_bounds__(384, 1)
         }
         mbar_expect_tx(&v_full[s], C::VTILE);
         for (int c = 0; c < C::NCHV; ++c)
-          tma_load_4d(smem + C::OFF_V + s * C::VTILE + c * 16384, &tv, &v_full[s], p.vcol0 + c * 64, j * 128, hkv,
-                      b);
+          tma_load_4d_hint(smem + C::OFF_V + s * C::VTILE + c * 16384, &tv, &v_full[s], p.vcol0 + c * 64, j * 128,
+                           hkv, b, pol_kv);
         loads[s] = use * 2 + 2;
       }
       // Never leave the CTA with a TMA write in flight: wait for the last load
@@ -493,8 +498,8 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
               for (int q4 = 0; q4 < 4; ++q4) {
                 if (c0 + q4 * 8 < dlim)
-                  *reinterpret_cast<uint4*>(orow + c0 + q4 * 8) =
-                      make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+                  __stcs(reinterpret_cast<uint4*>(orow + c0 + q4 * 8),
+                         make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]));  // streaming (evict first)
               }
             } else {
               const uint16_t* h = reinterpret_cast<const uint16_t*>(w);
