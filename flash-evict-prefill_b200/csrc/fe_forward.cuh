@@ -338,29 +338,32 @@ __global__ void __launch_bounds__(384, 1)
       const uint32_t v_addr = smem_u32(smem + C::OFF_V);
       // Descriptors are computed once; a k-step or a stage only moves the
       // start-address field (address >> 4 in the low 14 bits), so it is a
-      // plain add on the 64-bit descriptor.
+      // plain 32-bit add on the descriptor's low word.
       const uint64_t dq = smem_desc_sw128(q_addr, 16, 1024);
       const uint64_t dk = smem_desc_sw128(k_addr, 16, 1024);
       const uint64_t dv = smem_desc_sw128(v_addr, 16384, 1024);
       constexpr uint64_t TILE16 = C::TILE >> 4;
       constexpr uint64_t VTILE16 = C::VTILE >> 4;
+      const uint32_t dq_hi = static_cast<uint32_t>(dq >> 32), dk_hi = static_cast<uint32_t>(dk >> 32);
+      const uint32_t dv_hi = static_cast<uint32_t>(dv >> 32);
       auto issue_s = [&](int t, int s) {
-        const uint64_t a = dq + t * TILE16;
-        const uint64_t bb = dk + s * TILE16;
+        const uint32_t a = static_cast<uint32_t>(dq) + t * static_cast<uint32_t>(TILE16);
+        const uint32_t bb = static_cast<uint32_t>(dk) + s * static_cast<uint32_t>(TILE16);
         const uint32_t d = tmem + t * 128;
 #pragma unroll 8
         for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
-          umma_ss(d, a + off, bb + off, ID_S, kk > 0);
+          const uint32_t off = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+          umma_ss_lohi(d, a + off, dq_hi, bb + off, dk_hi, ID_S, kk > 0);
         }
       };
       auto issue_pv = [&](int t, int s, int j) {
-        const uint64_t bb = dv + s * VTILE16;
+        const uint32_t bb = static_cast<uint32_t>(dv) + s * static_cast<uint32_t>(VTILE16);
         const uint32_t d = tmem + 256 + t * DV;
         const uint32_t pa = tmem + t * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(d, pa + kk * 8, bb + static_cast<uint64_t>(kk * (2048 >> 4)), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ts_lohi(d, pa + kk * 8, bb + static_cast<uint32_t>(kk * (2048 >> 4)), dv_hi, ID_PV,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(q_full, 0, TO, abort_flag);

@@ -238,8 +238,10 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
     // ---------------------------------------------------------- MMA issuer --
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false);
-      const uint32_t k_addr = smem_u32(smem + C::OFF_K);
-      const uint32_t q_addr = smem_u32(smem + C::OFF_Q);
+      const uint64_t dk = smem_desc_sw128(smem_u32(smem + C::OFF_K), 16, 1024);
+      const uint64_t dq = smem_desc_sw128(smem_u32(smem + C::OFF_Q), 16, 1024);
+      const uint32_t dk_lo = static_cast<uint32_t>(dk), dk_hi = static_cast<uint32_t>(dk >> 32);
+      const uint32_t dq_lo = static_cast<uint32_t>(dq), dq_hi = static_cast<uint32_t>(dq >> 32);
       ReplayItems it;
       it.init(qt_lo, nqt, p.G, map);
       if (it.valid()) {
@@ -253,12 +255,13 @@ __global__ void __launch_bounds__(ReplayCfg<DP>::THREADS, ReplayCfg<DP>::CTAS_PE
           if (i >= C::NBUF) ok = mbar_wait(&s_free[sb], ((i / C::NBUF) - 1) & 1, TO, abort_flag);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t qa = q_addr + s * C::TILE;
+          // Descriptor low words step by (address offset >> 4); no carry leaves
+          // the 14-bit start-address field (shared memory is below 256 KB).
+          const uint32_t qa = dq_lo + static_cast<uint32_t>(s * (C::TILE >> 4));
 #pragma unroll
           for (int kk = 0; kk < DP / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_ss(tmem + sb * 128, smem_desc_sw128(k_addr + off, 16, 1024), smem_desc_sw128(qa + off, 16, 1024),
-                    ID_S, kk > 0);
+            const uint32_t off = static_cast<uint32_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+            umma_ss_lohi(tmem + sb * 128, dk_lo + off, dk_hi, qa + off, dq_hi, ID_S, kk > 0);
           }
           umma_commit(&s_full[sb]);
           umma_commit(&q_empty[s]);
