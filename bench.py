@@ -81,7 +81,7 @@ WORKLOADS = {
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # attention-forward launch of the c3 workload, from an ncu capture of this
 # kernel (not measured by this run; the JSON line says so).
-TRAFFIC_PER_FWD_LAUNCH = {"c3": 663745024 + 222873088}
+TRAFFIC_PER_FWD_LAUNCH = {"c3": 484338432 + 210992128}
 
 
 def peaks():
