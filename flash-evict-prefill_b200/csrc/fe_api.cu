@@ -17,12 +17,10 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
 #include "fe_forward.cuh"
-#include "fe_forward_pair.cuh"
 #include "fe_gather.cuh"
 #include "fe_replay.cuh"
 #include "fe_select.cuh"
@@ -296,58 +294,6 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   return FE_STATUS_OK;
 }
 
-// Pair-kernel variant of the attention launch (heads of 65-128 channels, no
-// block list): clusters of two CTAs, `pairs` clusters.
-template <bool BF16>
-int launch_fwd_pair(const CUtensorMap& tq, const CUtensorMap& tkh, const CUtensorMap& tv, const fe::FwdParams& p,
-                    int64_t pairs, cudaStream_t stream) {
-  using C = fe::FwdPairCfg;
-  auto kern = fe::fe_fwd_pair_kernel<BF16>;
-  int rc = set_smem(kern, C::SMEM);
-  if (rc) return rc;
-  static std::atomic<int> checked_regs{0};
-  int regs = checked_regs.load(std::memory_order_relaxed);
-  if (regs == 0) {
-    cudaFuncAttributes fa;
-    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
-    regs = fa.numRegs;
-    checked_regs.store(regs, std::memory_order_relaxed);
-  }
-  if (regs < fe::FWD_REGS_NEEDED)
-    return fail(FE_STATUS_UNSUPPORTED, "attention kernel compiled with %d registers/thread, needs %d", regs,
-                fe::FWD_REGS_NEEDED);
-  if (pairs * 2 > 0x7fffffff) return fail(FE_STATUS_UNSUPPORTED, "grid too large");
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3((unsigned)(pairs * 2));
-  cfg.blockDim = dim3(C::THREADS);
-  cfg.dynamicSmemBytes = (size_t)C::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tq, tkh, tv, p);
-  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
-  return FE_STATUS_OK;
-}
-
-// Attention kernel for 65-128-channel heads without a block list: CTA pairs
-// only with FE_ATTENTION_PAIRS=1 in the environment (read once).  Measured
-// bitwise equal to fe_fwd_kernel and slower (c3 7.76 vs 6.94 ms, c5 2.69 vs
-// 2.23 ms, c2 0.645 vs 0.503 ms), so off by default.
-bool use_pair_attention() {
-  static const bool on = [] {
-    const char* e = getenv("FE_ATTENTION_PAIRS");
-    return e != nullptr && e[0] == '1';
-  }();
-  return on;
-}
-
 template <bool BF16, int DP>
 int launch_replay(const CUtensorMap& tq, const CUtensorMap& tk, const fe::ReplayParams& p, int64_t items,
                   cudaStream_t stream) {
@@ -577,14 +523,6 @@ int fe_attention_fwd(const void* q, const int64_t* q_strides, const void* k, con
     p.vcol0 = 128;
     return dtype == FE_DTYPE_BF16 ? launch_fwd<true, 256, 128>(tq, tk, tv, p, items, s)
                                   : launch_fwd<false, 256, 128>(tq, tk, tv, p, items, s);
-  }
-  if (dp == 128 && !query_blocks && use_pair_attention()) {
-    CUtensorMap tkh;  // K in 64-key boxes: each CTA of a pair loads half of a KV tile's keys
-    if ((rc = make_map(&tkh, k, k_strides, batch, kv_heads, tokens, channels, dtype, "k", 64))) return rc;
-    p.num_blocks = (int)((tokens + fe::FwdPairCfg::BLOCK_ROWS - 1) / fe::FwdPairCfg::BLOCK_ROWS);
-    const int64_t pairs = (int64_t)p.num_blocks * batch * q_heads;
-    return dtype == FE_DTYPE_BF16 ? launch_fwd_pair<true>(tq, tkh, tv, p, pairs, s)
-                                  : launch_fwd_pair<false>(tq, tkh, tv, p, pairs, s);
   }
   if (dtype == FE_DTYPE_BF16)
     return dp == 64 ? launch_fwd<true, 64, 64>(tq, tk, tv, p, items, s)

@@ -235,125 +235,6 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// ------------------------------------------------ CTA pairs (cta_group::2) --
-// Two CTAs of a cluster whose ranks differ in bit 0 form a pair: one thread
-// of the even CTA issues M = 256 MMAs whose A rows (and D lanes) are split
-// between the two SMs (128 each) and whose B operand is split along N, each
-// CTA holding its half at the same shared-memory offset.  Every tcgen05
-// instruction of a kernel that uses pairs carries cta_group::2.
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Address of the same shared-memory offset in CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-
-// Every thread of every CTA of the cluster (release / acquire at cluster
-// scope); the non-aligned form, so it may follow divergent role code.
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Arrive on an mbarrier given by its shared::cluster address (this CTA's or a
-// peer's), releasing this thread's prior writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait for a barrier that threads of the peer CTA arrive on: acquire
-// at cluster scope, same bounds as mbar_wait.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t timeout_ns,
-                                                  volatile int* abort_flag) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  uint32_t it = 0;
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((++it & 63u) == 0) {
-      if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > timeout_ns) {
-        raise_status(FE_STATUS_TIMEOUT);
-        if (abort_flag != nullptr) *abort_flag = 1;
-        return false;
-      }
-    }
-  }
-}
-
-// 4-D tiled load into this CTA's shared memory whose completion is counted
-// on an mbarrier of either CTA of the pair (shared::cluster address).  No
-// cluster multicast: each CTA loads its own half of a pair's operands.
-__device__ __forceinline__ void tma_load_4d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
-                                                 int c0, int c1, int c2, int c3, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster), "l"(policy)
-      : "memory");
-}
-
-// TMEM allocation shared by the pair: one warp of each CTA (same warp index)
-// executes these together.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// Pair MMAs (issued by one thread of the even CTA), descriptors as lo/hi words.
-__device__ __forceinline__ void umma_pair_ss_lohi(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
-                                                  uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
-      "mov.b64 ad, {%1, %2};\n\t"
-      "mov.b64 bd, {%3, %4};\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %5, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void umma_pair_ts_lohi(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
-                                                  uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
-      "mov.b64 bd, {%2, %3};\n\t"
-      "setp.ne.b32 p, %5, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %4, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive once on the mbarrier at `cluster_addr` (this CTA's or the peer's)
-// when every pair MMA issued so far by this thread has completed.
-__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile.
 // K-major tiles: rows of 64 16-bit elements (128 B), 8-row groups 1024 B apart
 // (SBO); LBO unused. MN-major tiles: LBO = distance between 64-element MN
