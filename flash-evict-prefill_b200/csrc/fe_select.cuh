@@ -19,7 +19,8 @@
 // (budget-recent)-th largest key is found MSB-first with four 8-bit radix
 // passes whose histograms are merged through distributed shared memory.
 // Compaction walks each slice in index order (ballot/popc scans), so indices
-// come out already sorted; the cluster exchanges per-CTA counts for offsets.
+// come out already sorted; each CTA takes its output offset from the pass
+// histograms of the CTAs before it (read through distributed shared memory).
 // Optionally the same launch compacts K and V into dense [rows, budget,
 // channels] buffers: once every CTA of the cluster has written its indices
 // (a cluster barrier orders them), CTA r copies the rows of output positions
@@ -101,6 +102,47 @@ __device__ __forceinline__ int block_flag_scan(bool flag, int* warp_sums, int* t
   return res;
 }
 
+// Block-wide exclusive scan of one small count per thread in thread order.
+// Returns this thread's exclusive prefix; *total receives the block sum.
+__device__ __forceinline__ int block_count_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = (lane < SEL_WARPS) ? warp_sums[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    if (lane < SEL_WARPS) warp_sums[32 + lane] = wi - w;
+    if (lane == 31) warp_sums[64] = wi;
+  }
+  __syncthreads();
+  const int res = warp_sums[32 + warp] + incl - v;
+  *total = warp_sums[64];
+  __syncthreads();
+  return res;
+}
+
+// Split cluster barrier: arrive after this CTA's last read of another CTA's
+// shared memory, wait before leaving, so no CTA exits while a peer still
+// reads its histograms.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // After the row's indices are complete (every CTA of the cluster calls this
 // once, after its last index store), copy the K/V rows of this CTA's share of
 // the output positions.  The cluster barrier (release/acquire at cluster
@@ -131,12 +173,11 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
   const int64_t row = cl_index - static_cast<int64_t>(pi) * L.rows;
   const SelectParams& p = L.pol[pi];
 
-  extern __shared__ uint32_t keys[];
+  extern __shared__ __align__(16) uint32_t keys[];
   __shared__ uint32_t hist[2][256];
   __shared__ uint32_t tot[256];
   __shared__ int warp_sums[72];
   __shared__ uint32_t sel_digit, sel_krem, sel_done;
-  __shared__ long long counts[2];  // this CTA's {greater, equal} counts
 
   const int64_t N = p.N;
   const int64_t P = N - p.recent;
@@ -199,6 +240,14 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     // ---- radix select of the kk-th largest key over the whole cluster ----
     uint32_t prefix = 0, pmask = 0;
     uint32_t krem = static_cast<uint32_t>(kk);
+    // Keys of the CTAs before this one (cluster rank < crank) that are above
+    // the threshold, counted per digit from the same histograms the pass
+    // totals are made of: at every pass, the keys whose digit exceeds the
+    // selected one (thread d < 256 keeps digit d's share).  The keys of the
+    // final bucket (equal to the threshold, or the whole kept bucket when the
+    // passes stop early) are counted separately: earlier CTAs, whole cluster.
+    uint32_t gt_bef_d = 0;
+    __shared__ uint32_t fin_bef, fin_tot;
     if (threadIdx.x == 0) sel_done = 0u;
     for (int pass = 0; pass < 4; ++pass) {
       const int buf = pass & 1;
@@ -222,9 +271,14 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
           atomicAdd(&hist[buf][digit], static_cast<uint32_t>(__popc(peers)));
       }
       cluster.sync();
+      uint32_t bef_d = 0;
       if (threadIdx.x < 256) {
         uint32_t s = 0;
-        for (int rr = 0; rr < C; ++rr) s += cluster.map_shared_rank(&hist[buf][0], rr)[threadIdx.x];
+        for (int rr = 0; rr < C; ++rr) {
+          const uint32_t h = cluster.map_shared_rank(&hist[buf][0], rr)[threadIdx.x];
+          s += h;
+          if (rr < crank) bef_d += h;
+        }
         tot[threadIdx.x] = s;
       }
       __syncthreads();
@@ -262,6 +316,13 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       pmask |= 255u << shift;
       krem = sel_krem;
       const bool done = sel_done != 0u;
+      if (threadIdx.x < 256) {
+        if (threadIdx.x > sel_digit) gt_bef_d += bef_d;
+        if (threadIdx.x == sel_digit) {
+          fin_bef = bef_d;
+          fin_tot = tot[threadIdx.x];
+        }
+      }
       __syncthreads();
       if (done) {
         // The bucket holding the kk-th largest key is kept whole: every key
@@ -273,63 +334,67 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
     const uint32_t T = prefix;    // the kk-th largest key, or the kept bucket's floor
     const uint32_t need_eq = krem; // how many keys equal to T are kept (lowest indices)
 
-    // ---- per-CTA counts, exchanged for offsets ----
-    int gt = 0, eq = 0;
-    for (int i = threadIdx.x; i < len; i += SEL_THREADS) {
-      const uint32_t k = key_at(i);
-      gt += k > T;
-      eq += k == T;
-    }
+    // Every read of another CTA's histograms is behind us.
+    cluster_arrive_release();
+
+    // ---- offsets of this CTA's kept keys (from the pass histograms) ----
+    long long gt_before, eq_before, eq_total;
     {
-      __shared__ int red[2][SEL_WARPS];
-      const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        gt += __shfl_xor_sync(0xffffffffu, gt, o);
-        eq += __shfl_xor_sync(0xffffffffu, eq, o);
-      }
-      if (lane == 0) {
-        red[0][warp] = gt;
-        red[1][warp] = eq;
-      }
+      uint32_t v = threadIdx.x < 256 ? gt_bef_d : 0u;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if ((threadIdx.x & 31) == 0 && threadIdx.x < 256) warp_sums[threadIdx.x >> 5] = static_cast<int>(v);
       __syncthreads();
-      if (threadIdx.x == 0) {
-        long long tg = 0, te = 0;
-        for (int w = 0; w < SEL_WARPS; ++w) {
-          tg += red[0][w];
-          te += red[1][w];
-        }
-        counts[0] = tg;
-        counts[1] = te;
-      }
+      long long g = 0;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) g += static_cast<uint32_t>(warp_sums[w]);
+      gt_before = g;
+      eq_before = fin_bef;
+      eq_total = fin_tot;
+      __syncthreads();
     }
-    cluster.sync();
-    long long gt_before = 0, eq_before = 0, eq_total = 0;
-    for (int rr = 0; rr < C; ++rr) {
-      const long long* rc = cluster.map_shared_rank(&counts[0], rr);
-      if (rr < crank) {
-        gt_before += rc[0];
-        eq_before += rc[1];
-      }
-      eq_total += rc[1];
-    }
-    // Keep remote CTAs' shared memory alive until everyone has read it.
-    cluster.sync();
 
     // ---- ordered compaction ----
     if (eq_total <= static_cast<long long>(need_eq)) {
       // Every key equal to T is kept (the usual case: no tie is cut at the
       // threshold), so kept == (k >= T) and one scan per tile places it.
+      // Four consecutive keys per thread, one block scan per 4096 keys.
       long long run = gt_before + eq_before;
-      for (int base = 0; base < len; base += SEL_THREADS) {
-        const int i = base + threadIdx.x;
-        const bool in = i < len;
-        const bool kept = in && key_at(i) >= T;
+      for (int base = 0; base < len; base += 4 * SEL_THREADS) {
+        const int i0 = base + 4 * static_cast<int>(threadIdx.x);
+        uint32_t k4[4];
+        if constexpr (SMEM_KEYS) {
+          if (i0 + 3 < len) {
+            const uint4 q = *reinterpret_cast<const uint4*>(&keys[i0]);
+            k4[0] = q.x;
+            k4[1] = q.y;
+            k4[2] = q.z;
+            k4[3] = q.w;
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) k4[u] = (i0 + u < len) ? keys[i0 + u] : 0u;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) k4[u] = (i0 + u < len) ? key_at(i0 + u) : 0u;
+        }
+        bool kept[4];
+        int cnt = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          kept[u] = (i0 + u < len) && k4[u] >= T;
+          cnt += kept[u] ? 1 : 0;
+        }
         int tot_kept;
-        const int pos = block_flag_scan(kept, warp_sums, &tot_kept);
-        if (in) {
-          if (kept) out_idx[run + pos] = lo + i;
-          out_mask[lo + i] = kept ? keep_v : evict_v;
+        const int pos = block_count_scan(cnt, warp_sums, &tot_kept);
+        int w = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = i0 + u;
+          if (i < len) {
+            if (kept[u]) out_idx[run + pos + w++] = lo + i;
+            out_mask[lo + i] = kept[u] ? keep_v : evict_v;
+          }
         }
         run += tot_kept;
       }
@@ -358,6 +423,7 @@ __global__ void __launch_bounds__(SEL_THREADS, 1) fe_select_kernel(const __grid_
       run_eq += tot_eq;
     }
     }
+    cluster_wait_acquire();
   }
 
   // ---- K/V compaction, an equal share of the output per CTA ----
