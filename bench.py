@@ -461,8 +461,10 @@ def scoring_overhead(dev):
 
 def sharded_section(args, world, rank, local, dev, barrier):
     """The partitioned configurations at this world size: c4 query-sharded
-    (row-statistics exchange + one all_reduce of the FP32 scores) and c5
-    head-sharded (no collective); at world 1 both run as plain evict().
+    (row-statistics exchange + one all_reduce of the FP32 scores), c5
+    head-sharded (no collective) and, at world > 1, c4 head-sharded (its KV
+    heads split over the ranks, no collective: the control for the
+    query-sharded plan); at world 1 c4 and c5 run as plain evict().
     Every rank checks its part bit for bit against a single-GPU evict() of
     the same inputs on its own GPU.  Times are the maximum over ranks."""
     import torch.distributed as dist
@@ -479,8 +481,8 @@ def sharded_section(args, world, rank, local, dev, barrier):
         return t.tolist()
 
     result = {}
-    for name in ("c4", "c5"):
-        w = WORKLOADS[name]
+    for name in ("c4", "c5") + (("c4_heads",) if world > 1 else ()):
+        w = WORKLOADS["c4" if name == "c4_heads" else name]
         q, k, v = make_inputs(w, 2000, dev, on_device=True)
         kw = dict(w["kw"])
         budget = w["budget"]
@@ -488,7 +490,7 @@ def sharded_section(args, world, rank, local, dev, barrier):
         pool = kw.pop("pool_kernel", 1)
         kw["causal"] = w["causal"]
         g = w["hq"] // w["hkv"]
-        mode = "query" if name == "c4" else "heads"
+        mode = "query" if name == "c4" else "heads"  # c5 and c4_heads: (batch, kv-head) units
         runs = head_blocks(w["b"], w["hkv"], world)[rank]
 
         def step(marks=None):
@@ -500,7 +502,7 @@ def sharded_section(args, world, rank, local, dev, barrier):
             return [_evict_impl(q[b0:b1, h0 * g:h1 * g], k[b0:b1, h0:h1], v[b0:b1, h0:h1], budget, 0, recent,
                                 pool, marks, kw) for b0, b1, h0, h1 in runs]
 
-        steps = max(3, min(args.steps, 10 if name == "c4" else 20))
+        steps = max(3, min(args.steps, 20 if name == "c5" else 10))
         for _ in range(3):
             step()
         barrier()
