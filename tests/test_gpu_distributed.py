@@ -230,3 +230,34 @@ def test_head_sharded_ranks_on_one_gpu_match_single_gpu(monkeypatch, world):
             assert torch.equal(o, ref[0][b0:b1, h0:h1]) and torch.equal(i, ref[1][b0:b1, h0:h1])
             assert torch.equal(ix, ref[2][b0:b1, h0:h1]) and torch.equal(m, ref[3][b0:b1, h0:h1])
     assert covered.eq(1).all()
+
+
+@pytest.mark.parametrize("world", [3, 8])
+def test_head_sharded_c4_ranks_on_one_gpu_match_single_gpu(monkeypatch, world):
+    """The control plan for BASELINE c4 (B1 Hq32 Hkv8 N131072 D128 bf16,
+    causal, decay 0.1, reserved 64, budget 1024): its KV heads split over
+    `world` thread ranks on one GPU with evict_head_sharded, each rank's
+    outputs (its KV heads' 4 query heads each), importance, indices and mask
+    bitwise equal to one evict() of the whole tensor."""
+    from flash_evict import evict
+    from flash_evict.distributed import evict_head_sharded
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(23)
+    q = torch.randn(1, 32, 131072, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, 8, 131072, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, 8, 131072, 128, generator=g, device=dev).to(torch.bfloat16)
+    kw = dict(reserved_recent=64, recency_decay=0.1)
+    ref = evict(q, k, v, 1024, **kw)
+    torch.cuda.synchronize()
+    ranks = _ThreadRanks(world)
+    _patch_ranks(monkeypatch, ranks)
+    res = ranks.run(lambda r, grp: evict_head_sharded(q, k, v, 1024, group=grp, **kw))
+    torch.cuda.synchronize()
+    covered = torch.zeros(1, 8, dtype=torch.int32)
+    for r in range(world):
+        for b0, b1, h0, h1, o, i, ix, m in res[r]:
+            covered[b0:b1, h0:h1] += 1
+            assert torch.equal(o, ref[0][b0:b1, h0 * 4:h1 * 4]), f"rank {r}: output rows differ"
+            assert torch.equal(i, ref[1][b0:b1, h0:h1]), f"rank {r}: importance differs"
+            assert torch.equal(ix, ref[2][b0:b1, h0:h1]) and torch.equal(m, ref[3][b0:b1, h0:h1])
+    assert covered.eq(1).all()
